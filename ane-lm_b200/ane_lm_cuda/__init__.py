@@ -1,0 +1,204 @@
+"""Python access to libane_cuda.so, the sm_100a backend of ANE-LM's layer-op,
+sampler and BF16->FP16 convert path.
+
+``lib()`` returns the ctypes handle of the C ABI (include/ane_cuda.h).  The
+wrappers below take torch CUDA tensors, check shapes / dtypes / devices and
+pass raw device pointers and torch's current stream.  There is no fallback:
+if the shared library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REPO = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libane_cuda.so")
+HEADER = os.path.join(REPO, "include", "ane_cuda.h")
+
+OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+F32, F16, BF16 = 0, 1, 2
+FLAG_BAD_TOKEN_ID = 0x1
+
+_p = C.c_void_p
+_i64 = C.c_int64
+_i = C.c_int
+_f = C.c_float
+
+_SIGS = {
+    "ane_cuda_abi_version": (_i, []),
+    "ane_cuda_status_string": (C.c_char_p, [_i]),
+    "ane_cuda_last_error": (C.c_char_p, []),
+    "ane_cuda_read_status_flags": (_i, [C.POINTER(C.c_uint32), _i]),
+    "ane_cuda_bf16_to_f16": (_i, [_p, _p, _i64, _p]),
+    "ane_cuda_embedding_gather": (_i, [_p, _i, _p, _i, _p, _i64, _i, _i, _p]),
+    "ane_cuda_residual_rmsnorm": (_i, [_i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _f, _p]),
+    "ane_cuda_qk_norm_rope": (_i, [_i, _p, _p, _i64, _i64, _i, _i, _i, _i, _i, _i, _p, _p, _p,
+                                   _i64, _f, _f, _p]),
+    "ane_cuda_apply_rope_cached": (_i, [_p, _p, _i, _i, _i, _i, _i, _i, _i, _f, _p, _p, _p]),
+    "ane_cuda_silu_mul": (_i, [_i, _p, _i64, _p, _i64, _p, _i64, _i64, _i, _p]),
+    "ane_cuda_silu_inplace": (_i, [_i, _p, _i64, _p]),
+    "ane_cuda_mul_sigmoid_inplace": (_i, [_i, _p, _p, _i64, _p]),
+    "ane_cuda_softmax_rows": (_i, [_p, _i64, _i, _i64, _p]),
+    "ane_cuda_sample_rows": (_i, [_p, _i64, _i, _i64, _p, _p, _i64, _p, _f, _f, _i, _f, _p, _p]),
+}
+
+_lib = None
+
+
+class AneCudaError(RuntimeError):
+    def __init__(self, fn: str, status: int, msg: str):
+        super().__init__(f"{fn}: status {status}: {msg}")
+        self.status = status
+
+
+def lib() -> C.CDLL:
+    """The loaded C ABI.  Raises if libane_cuda.so has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {HERE}` "
+                              "(or __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def declared_symbols() -> list[str]:
+    """Every ane_cuda_* function declared in include/ane_cuda.h."""
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"ANE_CUDA_API\s+[\w\s\*]*?\b(ane_cuda_\w+)\s*\(", text)))
+
+
+def _check(fn: str, st: int):
+    if st != OK:
+        raise AneCudaError(fn, st, lib().ane_cuda_last_error().decode())
+
+
+# --------------------------------------------------------------------------
+# torch-tensor wrappers
+# --------------------------------------------------------------------------
+def _torch():
+    import torch
+    return torch
+
+
+def _dt(t) -> int:
+    torch = _torch()
+    m = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+    if t.dtype not in m:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return m[t.dtype]
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(t):
+    torch = _torch()
+    return C.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("tensors must be on a CUDA device")
+
+
+def read_status_flags(clear: bool = True) -> int:
+    v = C.c_uint32(0)
+    _check("read_status_flags", lib().ane_cuda_read_status_flags(C.byref(v), int(clear)))
+    return v.value
+
+
+def bf16_to_f16(inp, out=None):
+    """inp: int16/uint16/bfloat16 tensor of BF16 bits -> int16 tensor of FP16 bits."""
+    torch = _torch()
+    _cuda(inp)
+    inp = inp.contiguous()
+    if out is None:
+        out = torch.empty(inp.shape, dtype=torch.int16, device=inp.device)
+    _check("bf16_to_f16", lib().ane_cuda_bf16_to_f16(_ptr(out), _ptr(inp), inp.numel(), _stream(inp)))
+    return out
+
+
+def embedding_gather(table, ids, out_dtype=None, out=None):
+    torch = _torch()
+    _cuda(table, ids)
+    vocab, hidden = table.shape
+    odt = table.dtype if out_dtype is None else out_dtype
+    if out is None:
+        out = torch.empty((ids.numel(), hidden), dtype=odt, device=table.device)
+    ids = ids.to(torch.int32).contiguous()
+    _check("embedding_gather", lib().ane_cuda_embedding_gather(
+        _ptr(out), _dt(out), _ptr(table), _dt(table), _ptr(ids), ids.numel(), vocab, hidden,
+        _stream(table)))
+    return out
+
+
+def residual_rmsnorm(x, d, weight, out=None, eps=1e-6):
+    """x += d (in place, when d is given); returns rmsnorm(x) * weight."""
+    torch = _torch()
+    _cuda(x, d, weight)
+    rows, dim = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    _check("residual_rmsnorm", lib().ane_cuda_residual_rmsnorm(
+        _dt(x), _ptr(x), x.stride(0), _ptr(d), 0 if d is None else d.stride(0), _ptr(out),
+        out.stride(0), _ptr(weight), rows, dim, eps, _stream(x)))
+    return out
+
+
+def qk_norm_rope(qkv, q_weight, k_weight, positions, n_q_heads, n_kv_heads, head_dim,
+                 theta=1e6, eps=1e-6, rot_dim=None):
+    """In place on the q and k heads of qkv [rows, (n_q + 2 n_kv) * head_dim]."""
+    _cuda(qkv, q_weight, k_weight, positions)
+    rows, width = qkv.shape
+    es = qkv.element_size()
+    k = C.c_void_p(qkv.data_ptr() + n_q_heads * head_dim * es)
+    rot = head_dim if rot_dim is None else rot_dim
+    _check("qk_norm_rope", lib().ane_cuda_qk_norm_rope(
+        _dt(qkv), _ptr(qkv), k, qkv.stride(0), qkv.stride(0), head_dim, head_dim, n_q_heads,
+        n_kv_heads, head_dim, rot, _ptr(q_weight), _ptr(k_weight), _ptr(positions), rows, theta,
+        eps, _stream(qkv)))
+    return qkv
+
+
+def silu_mul(gate, up, out=None):
+    torch = _torch()
+    _cuda(gate, up)
+    rows, n = gate.shape
+    if out is None:
+        out = torch.empty_like(gate)
+    _check("silu_mul", lib().ane_cuda_silu_mul(
+        _dt(gate), _ptr(out), out.stride(0), _ptr(gate), gate.stride(0), _ptr(up), up.stride(0),
+        rows, n, _stream(gate)))
+    return out
+
+
+def softmax_rows(x):
+    _cuda(x)
+    rows, n = x.shape
+    _check("softmax_rows", lib().ane_cuda_softmax_rows(_ptr(x), rows, n, x.stride(0), _stream(x)))
+    return x
+
+
+def sample_rows(logits, uniforms, history=None, history_len=None, temperature=0.6,
+                repetition_penalty=1.2, repetition_context=256, frequency_penalty=0.1, out=None):
+    torch = _torch()
+    _cuda(logits, uniforms, history, history_len)
+    rows, vocab = logits.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    hs = 0 if history is None else history.stride(0)
+    _check("sample_rows", lib().ane_cuda_sample_rows(
+        _ptr(logits), rows, vocab, logits.stride(0), _ptr(history), _ptr(history_len), hs,
+        _ptr(uniforms), temperature, repetition_penalty, repetition_context, frequency_penalty,
+        _ptr(out), _stream(logits)))
+    return out

@@ -1,0 +1,163 @@
+// cuda_ops.cpp -- the reference-signature layer over the C ABI.
+#include "cuda_ops.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstdlib>
+
+namespace ane_lm {
+namespace cuda {
+
+namespace {
+
+thread_local void* t_stream = nullptr;
+thread_local int t_status = ANE_CUDA_OK;
+
+int note(const char* fn, int st) {
+    t_status = st;
+    if (st != ANE_CUDA_OK) fprintf(stderr, "ane_lm::cuda::%s: %s\n", fn, ane_cuda_last_error());
+    return st;
+}
+
+// Per-thread device staging for sample_token: history ids, the uniform and
+// the result.  Grown on demand, kept for the thread's lifetime.
+struct SampleStage {
+    int device = -1;
+    size_t cap = 0;
+    unsigned char* dev = nullptr;
+    ~SampleStage() {
+        if (dev) cudaFree(dev);
+    }
+};
+thread_local SampleStage t_stage;
+
+}  // namespace
+
+void set_stream(void* s) { t_stream = s; }
+void* stream() { return t_stream; }
+int last_status() { return t_status; }
+const char* last_error() { return ane_cuda_last_error(); }
+
+void silu_vec_inplace(float* x, int n, float*) {
+    note("silu_vec_inplace", ane_cuda_silu_inplace(ANE_CUDA_F32, x, n, t_stream));
+}
+
+void mul_sigmoid_inplace(float* y, const float* z, int n, float*) {
+    note("mul_sigmoid_inplace", ane_cuda_mul_sigmoid_inplace(ANE_CUDA_F32, y, z, n, t_stream));
+}
+
+void rmsnorm(float* out, const float* x, const float* weight, int dim, float eps) {
+    note("rmsnorm", ane_cuda_residual_rmsnorm(ANE_CUDA_F32, const_cast<float*>(x), dim, nullptr, 0,
+                                              out, dim, weight, 1, dim, eps, t_stream));
+}
+
+void apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads, int head_dim,
+                       int q_head_stride, int k_head_stride, int rot_dim, int pos, float theta,
+                       const float* cos_row, const float* sin_row) {
+    note("apply_rope_cached",
+         ane_cuda_apply_rope_cached(q, k, n_q_heads, n_kv_heads, head_dim, q_head_stride,
+                                    k_head_stride, rot_dim, pos, theta, cos_row, sin_row, t_stream));
+}
+
+void softmax(float* x, int n) { note("softmax", ane_cuda_softmax_rows(x, 1, n, n, t_stream)); }
+
+int sample_token(const float* logits, int vocab_size, const SamplingParams& params,
+                 const std::vector<int>& recent_tokens) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        note("sample_token", ANE_CUDA_ERR_CUDA);
+        return -1;
+    }
+    const size_t nh = recent_tokens.size();
+    const size_t need = 64 + nh * sizeof(int32_t);
+    if (t_stage.device != dev || t_stage.cap < need) {
+        if (t_stage.dev) cudaFree(t_stage.dev);
+        t_stage.dev = nullptr;
+        t_stage.cap = 0;
+        size_t cap = need < 4096 ? 4096 : need * 2;
+        if (cudaMalloc(&t_stage.dev, cap) != cudaSuccess) {
+            fprintf(stderr, "ane_lm::cuda::sample_token: cudaMalloc of %zu bytes failed\n", cap);
+            t_status = ANE_CUDA_ERR_CUDA;
+            return -1;
+        }
+        t_stage.device = dev;
+        t_stage.cap = cap;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(t_stream);
+    int32_t* d_out = reinterpret_cast<int32_t*>(t_stage.dev);
+    float* d_u = reinterpret_cast<float*>(t_stage.dev + 16);
+    int32_t* d_len = reinterpret_cast<int32_t*>(t_stage.dev + 32);
+    int32_t* d_hist = reinterpret_cast<int32_t*>(t_stage.dev + 64);
+    const float r = (float)drand48();
+    const int32_t len = (int32_t)nh;
+    cudaError_t e = cudaMemcpyAsync(d_u, &r, sizeof(r), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d_len, &len, sizeof(len), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess && nh)
+        e = cudaMemcpyAsync(d_hist, recent_tokens.data(), nh * sizeof(int32_t),
+                            cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "ane_lm::cuda::sample_token: %s\n", cudaGetErrorString(e));
+        t_status = ANE_CUDA_ERR_CUDA;
+        return -1;
+    }
+    int st = ane_cuda_sample_rows(logits, 1, vocab_size, vocab_size, nh ? d_hist : nullptr,
+                                  nh ? d_len : nullptr, (int64_t)nh, d_u, params.temperature,
+                                  params.repetition_penalty, params.repetition_context_size,
+                                  params.frequency_penalty, d_out, s);
+    if (note("sample_token", st) != ANE_CUDA_OK) return -1;
+    int32_t tok = -1;
+    e = cudaMemcpyAsync(&tok, d_out, sizeof(tok), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        fprintf(stderr, "ane_lm::cuda::sample_token: %s\n", cudaGetErrorString(e));
+        t_status = ANE_CUDA_ERR_CUDA;
+        return -1;
+    }
+    return tok;
+}
+
+void bf16_to_f16_vec(uint16_t* out, const uint16_t* in, int n) {
+    note("bf16_to_f16_vec", ane_cuda_bf16_to_f16(out, in, n, t_stream));
+}
+
+void residual_rmsnorm(ane_cuda_dtype dtype, void* x, const void* d, void* out, const float* weight,
+                      int64_t rows, int dim, float eps) {
+    note("residual_rmsnorm", ane_cuda_residual_rmsnorm(dtype, x, dim, d, dim, out, dim, weight,
+                                                       rows, dim, eps, t_stream));
+}
+
+void qk_norm_rope(ane_cuda_dtype dtype, void* qkv, const float* q_weight, const float* k_weight,
+                  const int32_t* positions, int64_t rows, int n_q_heads, int n_kv_heads,
+                  int head_dim, float theta, float eps) {
+    const int64_t width = (int64_t)(n_q_heads + 2 * n_kv_heads) * head_dim;
+    const size_t es = dtype == ANE_CUDA_F32 ? 4 : 2;
+    void* k = static_cast<unsigned char*>(qkv) + (size_t)n_q_heads * head_dim * es;
+    note("qk_norm_rope", ane_cuda_qk_norm_rope(dtype, qkv, k, width, width, head_dim, head_dim,
+                                               n_q_heads, n_kv_heads, head_dim, head_dim, q_weight,
+                                               k_weight, positions, rows, theta, eps, t_stream));
+}
+
+void silu_mul(ane_cuda_dtype dtype, void* out, const void* gate, const void* up, int64_t rows,
+              int n) {
+    note("silu_mul", ane_cuda_silu_mul(dtype, out, n, gate, n, up, n, rows, n, t_stream));
+}
+
+void embedding_gather(void* out, ane_cuda_dtype out_dtype, const void* table,
+                      ane_cuda_dtype table_dtype, const int32_t* ids, int64_t rows, int vocab,
+                      int hidden) {
+    note("embedding_gather", ane_cuda_embedding_gather(out, out_dtype, table, table_dtype, ids,
+                                                       rows, vocab, hidden, t_stream));
+}
+
+void sample_rows(const float* logits, int64_t rows, int vocab, const int32_t* history,
+                 const int32_t* history_len, int64_t history_stride, const float* uniforms,
+                 const SamplingParams& p, int32_t* out_tokens) {
+    note("sample_rows", ane_cuda_sample_rows(logits, rows, vocab, vocab, history, history_len,
+                                             history_stride, uniforms, p.temperature,
+                                             p.repetition_penalty, p.repetition_context_size,
+                                             p.frequency_penalty, out_tokens, t_stream));
+}
+
+}  // namespace cuda
+}  // namespace ane_lm

@@ -1,0 +1,160 @@
+// ane_common.cuh -- device helpers shared by the sm_100a kernels of the
+// ANE-LM layer-op / sampler / convert path.
+//
+// Every floating-point step that the result depends on is written with an
+// explicit round-to-nearest intrinsic (__fmul_rn, __fadd_rn, __fmaf_rn,
+// __fdiv_rn, __fsqrt_rn) so that nvcc cannot contract or reassociate it;
+// the CPU restatement used by the tests performs the same operations in the
+// same order, which is what makes the results reproducible bit for bit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "ane_cuda.h"
+
+namespace ane {
+
+constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------
+// element types
+// ---------------------------------------------------------------------
+struct F32 {
+    using storage = float;
+    static constexpr int kVec = 4;  // elements per 16-byte vector
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+struct F16 {
+    using storage = __half;
+    static constexpr int kVec = 8;
+    static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+    static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+struct BF16 {
+    using storage = __nv_bfloat16;
+    static constexpr int kVec = 8;
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// Unpack / pack one 16-byte vector of T into / from kVec floats.
+template <typename T>
+__device__ __forceinline__ void unpack(const uint4& v, float* f) {
+    const typename T::storage* p = reinterpret_cast<const typename T::storage*>(&v);
+#pragma unroll
+    for (int i = 0; i < T::kVec; i++) f[i] = T::to_f(p[i]);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack(const float* f) {
+    uint4 v;
+    typename T::storage* p = reinterpret_cast<typename T::storage*>(&v);
+#pragma unroll
+    for (int i = 0; i < T::kVec; i++) p[i] = T::from_f(f[i]);
+    return v;
+}
+
+// 16-byte global accesses.  ld_stream / st_stream mark lines as touched
+// once (evict-first), for rows that are read or written exactly once.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    return __ldcs(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ void st_stream(void* p, const uint4& v) {
+    __stcs(reinterpret_cast<uint4*>(p), v);
+}
+__device__ __forceinline__ uint4 ld_keep(const void* p) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// ---------------------------------------------------------------------
+// exp: Cody & Waite (1980) reduction x = k ln2 + r, k = rint(x log2 e),
+// ln 2 as a float head + tail; Taylor series of e^r to degree 7 by Horner;
+// scaling by 2^k with at most two multiplies (the second one rounds once
+// into the subnormal range).  Constants: ln 2, log2 e and 1/n! rounded to
+// float.  Used where the result must be reproducible bit for bit (the
+// sampler's softmax).
+// ---------------------------------------------------------------------
+__device__ __forceinline__ float pow2i(int k) { return u2f((uint32_t)(k + 127) << 23); }
+
+__device__ __forceinline__ float pinned_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return u2f(0x7F800000u);
+    if (x < -104.0f) return 0.0f;
+    const float k = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-k, 0.693147182464599609375f, x);
+    r = __fmaf_rn(-k, -1.904654212125933608e-09f, r);
+    float p = __fmaf_rn(0.00019841270113829523324966431f, r, 0.0013888889225199818611145020f);
+    p = __fmaf_rn(p, r, 0.0083333337679505348205566406f);
+    p = __fmaf_rn(p, r, 0.041666667908430099487304688f);
+    p = __fmaf_rn(p, r, 0.16666667163372039794921875f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ki = (int)k;
+    if (ki > 127) return __fmul_rn(__fmul_rn(p, 2.0f), pow2i(127));
+    if (ki < -126) return __fmul_rn(__fmul_rn(p, pow2i(ki + 64)), pow2i(-64));
+    return __fmul_rn(p, pow2i(ki));
+}
+
+// ---------------------------------------------------------------------
+// sin / cos for RoPE: reduction by pi/2 in double (pi/2 as double head +
+// tail, two fma), reduced argument rounded to float, Taylor polynomials of
+// sin (degree 9) and cos (degree 10) in float by Horner, quadrant rotation.
+// ---------------------------------------------------------------------
+__device__ __forceinline__ void pinned_sincosf(float x, float* s, float* c) {
+    const double xd = (double)x;
+    const double kd = rint(__dmul_rn(xd, 0x1.45f306dc9c883p-1));
+    double rd = __fma_rn(-kd, 0x1.921fb54442d18p+0, xd);
+    rd = __fma_rn(-kd, 0x1.1a62633145c07p-54, rd);
+    const float r = __double2float_rn(rd);
+    const int q = (int)__dsub_rn(kd, __dmul_rn(4.0, floor(__dmul_rn(kd, 0.25))));
+    const float r2 = __fmul_rn(r, r);
+    float t = __fmaf_rn(2.7557318844628753e-06f, r2, -0.00019841270113829523324966431f);
+    t = __fmaf_rn(t, r2, 0.0083333337679505348205566406f);
+    t = __fmaf_rn(t, r2, -0.16666667163372039794921875f);
+    t = __fmul_rn(t, r2);
+    const float sp = __fmaf_rn(t, r, r);
+    float u = __fmaf_rn(-2.755731998149713e-07f, r2, 2.4801587642286904e-05f);
+    u = __fmaf_rn(u, r2, -0.0013888889225199818611145020f);
+    u = __fmaf_rn(u, r2, 0.041666667908430099487304688f);
+    u = __fmaf_rn(u, r2, -0.5f);
+    const float cp = __fmaf_rn(u, r2, 1.0f);
+    switch (q) {
+        case 0:  *s = sp;  *c = cp;  break;
+        case 1:  *s = cp;  *c = -sp; break;
+        case 2:  *s = -sp; *c = -cp; break;
+        default: *s = -cp; *c = sp;  break;
+    }
+}
+
+// Lane-partial fmaf chain of the pinned sum of squares (one chunk).
+template <int N>
+__device__ __forceinline__ float sumsq_chain(const float* v, float acc) {
+#pragma unroll
+    for (int i = 0; i < N; i++) acc = __fmaf_rn(v[i], v[i], acc);
+    return acc;
+}
+
+// xor butterfly over `width` lanes (offsets width/2 .. 1); every lane ends
+// with the same bits because IEEE addition is commutative.
+__device__ __forceinline__ float butterfly_sum(float v, int width) {
+    for (int off = width >> 1; off >= 1; off >>= 1)
+        v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+// inv = 1 / sqrtf(ss / dim + eps)   (core/cpu_ops.cpp:28)
+__device__ __forceinline__ float rms_inv(float ss, int dim, float eps) {
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace ane

@@ -1,0 +1,32 @@
+// ane_internal.h -- host-side helpers shared by the C ABI entry points.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ane_cuda.h"
+
+namespace ane {
+
+// Records a one-line description for ane_cuda_last_error() (thread-local)
+// and returns `status`.
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+
+// ANE_CUDA_OK, or ANE_CUDA_ERR_CUDA with the launch error recorded.
+int check_launch(const char* what);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool is_aligned(const void* p, uintptr_t a) {
+    return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+inline int elem_size(int dtype) { return dtype == ANE_CUDA_F32 ? 4 : 2; }
+inline bool valid_dtype(int dtype) {
+    return dtype == ANE_CUDA_F32 || dtype == ANE_CUDA_F16 || dtype == ANE_CUDA_BF16;
+}
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+}  // namespace ane

@@ -1,0 +1,91 @@
+// convert.cu -- BF16 -> FP16 weight conversion, bit-exact with the
+// reference's truncating bf16_to_f16 (include/ane_lm/common.h:58-75).
+//
+// HBM-bound streaming kernel: 2 bytes read + 2 bytes written per element.
+// Each thread moves 16-byte vectors (8 elements) with evict-first loads and
+// stores, UNROLL vectors in flight, over a grid sized to the SM count.
+#include "ane_common.cuh"
+#include "ane_internal.h"
+
+namespace ane {
+
+// One element: exponent re-bias by -112; e >= 31 (Inf/NaN included) ->
+// signed Inf; 1 <= e <= 30 -> e<<10 | top 7 mantissa bits << 3;
+// -10 <= e <= 0 -> (1.m << 16) >> (14 - e), i.e. the hidden-bit mantissa
+// shifted right by (1 - e) and then by 13, truncating; below -> signed 0.
+__device__ __forceinline__ uint32_t bf16_to_f16_bits(uint32_t b) {
+    const uint32_t sign = b & 0x8000u;
+    const int e = (int)((b >> 7) & 0xFFu) - 112;
+    const uint32_t m7 = b & 0x7Fu;
+    uint32_t r;
+    if (e >= 31)
+        r = 0x7C00u;
+    else if (e >= 1)
+        r = ((uint32_t)e << 10) | (m7 << 3);
+    else if (e >= -10)
+        r = ((m7 | 0x80u) << 16) >> (14 - e);
+    else
+        r = 0u;
+    return sign | r;
+}
+
+__device__ __forceinline__ uint32_t cvt_pair(uint32_t w) {
+    return bf16_to_f16_bits(w & 0xFFFFu) | (bf16_to_f16_bits(w >> 16) << 16);
+}
+
+__device__ __forceinline__ uint4 cvt_vec(uint4 v) {
+    return make_uint4(cvt_pair(v.x), cvt_pair(v.y), cvt_pair(v.z), cvt_pair(v.w));
+}
+
+constexpr int kConvThreads = 256;
+constexpr int kConvUnroll = 4;
+
+// Vector path: in/out 16-byte aligned, nvec 8-element vectors.
+__global__ void __launch_bounds__(kConvThreads)
+bf16_to_f16_vec_kernel(uint4* __restrict__ out, const uint4* __restrict__ in, int64_t nvec) {
+    const int64_t stride = (int64_t)gridDim.x * kConvThreads;
+    int64_t i = (int64_t)blockIdx.x * kConvThreads + threadIdx.x;
+    // Main loop: kConvUnroll independent vectors per thread in flight.
+    for (; i + (kConvUnroll - 1) * stride < nvec; i += kConvUnroll * stride) {
+        uint4 v[kConvUnroll];
+#pragma unroll
+        for (int u = 0; u < kConvUnroll; u++) v[u] = ld_stream(in + i + u * stride);
+#pragma unroll
+        for (int u = 0; u < kConvUnroll; u++) st_stream(out + i + u * stride, cvt_vec(v[u]));
+    }
+    for (; i < nvec; i += stride) st_stream(out + i, cvt_vec(ld_stream(in + i)));
+}
+
+// Scalar path for the ragged tail or unaligned buffers.
+__global__ void bf16_to_f16_scalar_kernel(uint16_t* __restrict__ out,
+                                          const uint16_t* __restrict__ in, int64_t n) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        out[i] = (uint16_t)bf16_to_f16_bits(in[i]);
+}
+
+}  // namespace ane
+
+extern "C" int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t n, void* stream) {
+    using namespace ane;
+    if (n < 0) return fail(ANE_CUDA_ERR_INVALID_ARG, "bf16_to_f16: n = %lld < 0", (long long)n);
+    if (n == 0) return ANE_CUDA_OK;
+    if (!out || !in) return fail(ANE_CUDA_ERR_INVALID_ARG, "bf16_to_f16: null pointer");
+    cudaStream_t s = as_stream(stream);
+    const int sms = sm_count();
+    int64_t done = 0;
+    if (is_aligned(out, 16) && is_aligned(in, 16) && n >= 8) {
+        const int64_t nvec = n / 8;
+        const int64_t want = (nvec + kConvThreads * kConvUnroll - 1) / (kConvThreads * kConvUnroll);
+        const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+        bf16_to_f16_vec_kernel<<<blocks, kConvThreads, 0, s>>>(
+            reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(in), nvec);
+        done = nvec * 8;
+    }
+    if (done < n) {
+        const int64_t rest = n - done;
+        const int blocks = (int)((rest + 255) / 256 < (int64_t)sms * 4 ? (rest + 255) / 256 : (int64_t)sms * 4);
+        bf16_to_f16_scalar_kernel<<<blocks, 256, 0, s>>>(out + done, in + done, rest);
+    }
+    return check_launch("bf16_to_f16");
+}

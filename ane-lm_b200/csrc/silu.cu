@@ -1,0 +1,168 @@
+// silu.cu -- SiLU-gated activation and its sigmoid relatives
+// (core/cpu_ops.cpp:7-23; the fused FFN gate of core/ane_runtime.cpp:393-395).
+//
+//   SILU_MUL    out = (g / (1 + exp(-g))) * u
+//   SILU        x   =  x / (1 + exp(-x))                 silu_vec_inplace
+//   MUL_SIGMOID y   =  y / (1 + exp(-z))                 mul_sigmoid_inplace
+//
+// Element-wise and HBM-bound: 16-byte vectors, evict-first accesses, a grid
+// sized to the SM count.  exp is the pinned Cody-Waite/Taylor exp and the
+// divide is IEEE, each step rounded on its own, as the reference's vneg /
+// vvexpf / vsadd / vdiv sequence.
+#include "ane_common.cuh"
+#include "ane_internal.h"
+
+namespace ane {
+
+enum ActMode { SILU_MUL = 0, SILU = 1, MUL_SIGMOID = 2 };
+
+template <int MODE>
+__device__ __forceinline__ float act(float a, float b) {
+    if constexpr (MODE == SILU_MUL) {
+        const float s = __fdiv_rn(a, __fadd_rn(1.0f, pinned_expf(-a)));
+        return __fmul_rn(s, b);
+    } else if constexpr (MODE == SILU) {
+        return __fdiv_rn(a, __fadd_rn(1.0f, pinned_expf(-a)));
+    } else {  // a = y, b = z
+        return __fdiv_rn(a, __fadd_rn(1.0f, pinned_expf(-b)));
+    }
+}
+
+constexpr int kActThreads = 256;
+
+struct ActArgs {
+    void* out;
+    const void* a;
+    const void* b;
+    int64_t out_stride, a_stride, b_stride;
+    int64_t rows;
+    int64_t n;
+};
+
+// Vector path: n % kVec == 0, every row 16-byte aligned.  Work item i is
+// vector (i % nvec) of row (i / nvec).
+template <typename T, int MODE, bool FLAT>
+__global__ void __launch_bounds__(kActThreads)
+act_vec_kernel(const ActArgs p) {
+    using S = typename T::storage;
+    constexpr int V = T::kVec;
+    const int64_t nvec = p.n / V;
+    const int64_t total = p.rows * nvec;
+    const int64_t stride = (int64_t)gridDim.x * kActThreads;
+    for (int64_t i = (int64_t)blockIdx.x * kActThreads + threadIdx.x; i < total; i += 2 * stride) {
+        uint4 av[2], bv[2];
+        int64_t r[2], c[2];
+        bool ok[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int64_t j = i + u * stride;
+            ok[u] = j < total;
+            if constexpr (FLAT) {
+                r[u] = 0;
+                c[u] = j * V;
+            } else {
+                r[u] = ok[u] ? j / nvec : 0;
+                c[u] = ok[u] ? (j - r[u] * nvec) * V : 0;
+            }
+            if (ok[u]) {
+                av[u] = ld_stream((const S*)p.a + r[u] * p.a_stride + c[u]);
+                if constexpr (MODE != SILU) bv[u] = ld_stream((const S*)p.b + r[u] * p.b_stride + c[u]);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            if (!ok[u]) continue;
+            float x[V], y[V];
+            unpack<T>(av[u], x);
+            if constexpr (MODE != SILU) unpack<T>(bv[u], y);
+#pragma unroll
+            for (int e = 0; e < V; e++) x[e] = act<MODE>(x[e], MODE != SILU ? y[e] : 0.0f);
+            st_stream((S*)p.out + r[u] * p.out_stride + c[u], pack<T>(x));
+        }
+    }
+}
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kActThreads)
+act_scalar_kernel(const ActArgs p) {
+    using S = typename T::storage;
+    const int64_t total = p.rows * p.n;
+    const int64_t stride = (int64_t)gridDim.x * kActThreads;
+    for (int64_t i = (int64_t)blockIdx.x * kActThreads + threadIdx.x; i < total; i += stride) {
+        const int64_t r = i / p.n, c = i - r * p.n;
+        const float x = T::to_f(((const S*)p.a)[r * p.a_stride + c]);
+        const float y = MODE != SILU ? T::to_f(((const S*)p.b)[r * p.b_stride + c]) : 0.0f;
+        ((S*)p.out)[r * p.out_stride + c] = T::from_f(act<MODE>(x, y));
+    }
+}
+
+template <typename T, int MODE>
+static int launch_act(ActArgs p, cudaStream_t s) {
+    constexpr int V = T::kVec;
+    const int es = (int)sizeof(typename T::storage);
+    bool vec = p.n % V == 0 && is_aligned(p.out, 16) && is_aligned(p.a, 16) &&
+               (p.out_stride * es) % 16 == 0 && (p.a_stride * es) % 16 == 0;
+    if (MODE != SILU) vec = vec && is_aligned(p.b, 16) && (p.b_stride * es) % 16 == 0;
+    // rows stored back to back: one flat run of rows * n elements
+    if (p.out_stride == p.n && p.a_stride == p.n && (MODE == SILU || p.b_stride == p.n)) {
+        p.n *= p.rows;
+        p.out_stride = p.a_stride = p.b_stride = p.n;
+        p.rows = 1;
+    }
+    const int64_t items = vec ? p.rows * (p.n / V) : p.rows * p.n;
+    const int64_t want = (items + 2 * kActThreads - 1) / (2 * kActThreads);
+    const int64_t cap = (int64_t)sm_count() * 8;
+    const int blocks = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    if (vec && p.rows == 1) act_vec_kernel<T, MODE, true><<<blocks, kActThreads, 0, s>>>(p);
+    else if (vec) act_vec_kernel<T, MODE, false><<<blocks, kActThreads, 0, s>>>(p);
+    else act_scalar_kernel<T, MODE><<<blocks, kActThreads, 0, s>>>(p);
+    return check_launch("activation");
+}
+
+template <int MODE>
+static int dispatch_act(int dtype, const ActArgs& p, cudaStream_t s) {
+    if (dtype == ANE_CUDA_F32) return launch_act<F32, MODE>(p, s);
+    if (dtype == ANE_CUDA_F16) return launch_act<F16, MODE>(p, s);
+    return launch_act<BF16, MODE>(p, s);
+}
+
+}  // namespace ane
+
+extern "C" {
+
+int ane_cuda_silu_mul(int dtype, void* out, int64_t out_stride, const void* gate,
+                      int64_t gate_stride, const void* up, int64_t up_stride, int64_t rows,
+                      int n, void* stream) {
+    using namespace ane;
+    if (!valid_dtype(dtype)) return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_mul: bad dtype %d", dtype);
+    if (rows < 0 || n <= 0)
+        return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_mul: rows=%lld n=%d", (long long)rows, n);
+    if (rows == 0) return ANE_CUDA_OK;
+    if (!out || !gate || !up) return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_mul: null pointer");
+    if (out_stride < n || gate_stride < n || up_stride < n)
+        return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_mul: row stride below n");
+    ActArgs p{out, gate, up, out_stride, gate_stride, up_stride, rows, n};
+    return dispatch_act<SILU_MUL>(dtype, p, as_stream(stream));
+}
+
+int ane_cuda_silu_inplace(int dtype, void* x, int64_t n, void* stream) {
+    using namespace ane;
+    if (!valid_dtype(dtype)) return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_inplace: bad dtype %d", dtype);
+    if (n < 0) return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_inplace: n=%lld", (long long)n);
+    if (n == 0) return ANE_CUDA_OK;
+    if (!x) return fail(ANE_CUDA_ERR_INVALID_ARG, "silu_inplace: null pointer");
+    ActArgs p{x, x, nullptr, n, n, 0, 1, n};
+    return dispatch_act<SILU>(dtype, p, as_stream(stream));
+}
+
+int ane_cuda_mul_sigmoid_inplace(int dtype, void* y, const void* z, int64_t n, void* stream) {
+    using namespace ane;
+    if (!valid_dtype(dtype)) return fail(ANE_CUDA_ERR_INVALID_ARG, "mul_sigmoid_inplace: bad dtype %d", dtype);
+    if (n < 0) return fail(ANE_CUDA_ERR_INVALID_ARG, "mul_sigmoid_inplace: n=%lld", (long long)n);
+    if (n == 0) return ANE_CUDA_OK;
+    if (!y || !z) return fail(ANE_CUDA_ERR_INVALID_ARG, "mul_sigmoid_inplace: null pointer");
+    ActArgs p{y, y, z, n, n, n, 1, n};
+    return dispatch_act<MUL_SIGMOID>(dtype, p, as_stream(stream));
+}
+
+}  // extern "C"

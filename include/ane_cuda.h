@@ -1,0 +1,149 @@
+/*
+ * ane_cuda.h -- C ABI of the B200 (sm_100a) backend for ANE-LM's non-matmul
+ * hot path: the layer ops of core/cpu_ops, the sampler of core/sampling and
+ * the BF16 -> FP16 weight conversion behind `ane-lm convert`.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer argument is a DEVICE pointer of the calling thread's
+ *     current CUDA device unless stated otherwise; the caller owns every
+ *     buffer.  In-place use is allowed where the reference allows it.
+ *   - Strides are in elements.  `stream` is a cudaStream_t (NULL = the
+ *     legacy default stream).  Calls are asynchronous on `stream`.
+ *   - The return value is an ane_cuda_status; ane_cuda_last_error() gives a
+ *     one-line description of the calling thread's last failure.
+ *   - Re-entrant: no call keeps state between calls except the per-device
+ *     status word read by ane_cuda_read_status_flags().
+ *
+ * Reference citations are file:line in the ANE-LM source tree.
+ */
+#ifndef ANE_CUDA_H
+#define ANE_CUDA_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ANE_CUDA_API __attribute__((visibility("default")))
+#else
+#define ANE_CUDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    ANE_CUDA_OK = 0,
+    ANE_CUDA_ERR_INVALID_ARG = 1, /* null pointer, bad size or stride        */
+    ANE_CUDA_ERR_UNSUPPORTED = 2, /* valid request this build does not cover */
+    ANE_CUDA_ERR_CUDA = 3         /* a CUDA runtime call or launch failed    */
+} ane_cuda_status;
+
+/* element types of activation rows and tables */
+typedef enum { ANE_CUDA_F32 = 0, ANE_CUDA_F16 = 1, ANE_CUDA_BF16 = 2 } ane_cuda_dtype;
+
+/* bits of the per-device status word */
+#define ANE_CUDA_FLAG_BAD_TOKEN_ID 0x1u /* a gather id was outside [0, vocab) */
+
+ANE_CUDA_API int ane_cuda_abi_version(void);
+ANE_CUDA_API const char* ane_cuda_status_string(int status);
+ANE_CUDA_API const char* ane_cuda_last_error(void);
+
+/* Reads (and, when clear != 0, resets) the status word of the current device.
+ * Synchronises the device. */
+ANE_CUDA_API int ane_cuda_read_status_flags(uint32_t* flags, int clear);
+
+/* ---- BF16 -> FP16 conversion ------------------------------------------
+ * Replaces bf16_to_f16_vec (include/ane_lm/common.h:81-83), i.e.
+ * bf16_to_f16 (:73-75) = f32_to_f16 (:58-71) of bf16_to_f32 (:21-26):
+ * TRUNCATING, exponent >= 31 (Inf and NaN included) -> signed Inf,
+ * below 2^-25 -> signed zero.  Bit-exact.  Call sites: write_ane_blob
+ * (core/safetensors.cpp:335) and build_weight_blob (core/ane_runtime.cpp:207). */
+ANE_CUDA_API int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t n, void* stream);
+
+/* ---- embedding gather --------------------------------------------------
+ * Replaces the row memcpy of Qwen3Model::forward (models/llm/qwen3.cpp:498),
+ * batched: out[r, :] = table[ids[r], :].  out_dtype equals table_dtype (a
+ * byte copy) or is F32 with an F16/BF16 table (exact widening).  An id
+ * outside [0, vocab) writes a zero row and sets ANE_CUDA_FLAG_BAD_TOKEN_ID. */
+ANE_CUDA_API int ane_cuda_embedding_gather(void* out, int out_dtype, const void* table, int table_dtype,
+                              const int32_t* ids, int64_t rows, int vocab, int hidden,
+                              void* stream);
+
+/* ---- residual add + RMSNorm -------------------------------------------
+ * Replaces rmsnorm (core/cpu_ops.cpp:25-31) fused with the residual add
+ * vDSP_vadd(x, d, x) that precedes it (models/llm/qwen3.cpp:516-518, :527,
+ * :503).  Per row: if d != NULL, x += d is stored back into x (in x's
+ * dtype); then out = (x * inv) * weight with inv = 1/sqrtf(sum(x^2)/dim +
+ * eps).  Without d this is rmsnorm(out, x, weight, dim, eps); out may alias x.
+ * dtype: F32, F16 or BF16 for x, d and out; weight is fp32 [dim]. */
+ANE_CUDA_API int ane_cuda_residual_rmsnorm(int dtype, void* x, int64_t x_stride, const void* d,
+                              int64_t d_stride, void* out, int64_t out_stride,
+                              const float* weight, int64_t rows, int dim, float eps,
+                              void* stream);
+
+/* ---- per-head QK-norm + RoPE ------------------------------------------
+ * Replaces the per-head rmsnorm of q and k (models/llm/qwen3.cpp:444-461)
+ * followed by apply_rope_cached (core/cpu_ops.cpp:56-80, half-split fast
+ * path :43-54; models/llm/qwen3.cpp:17-52, :463-473), in place, for a batch
+ * of rows each with its own position.  Head h of row r sits at
+ * q + r*q_row_stride + h*q_head_stride (k likewise).  cos/sin are computed
+ * in registers from inv_freq[j] = 1/powf(theta, 2j/rot_dim) (the table of
+ * models/llm/qwen3.cpp:200-219, without its 16384-position cap).
+ * q_weight / k_weight (fp32 [head_dim]) may both be NULL: RoPE only. */
+ANE_CUDA_API int ane_cuda_qk_norm_rope(int dtype, void* q, void* k, int64_t q_row_stride,
+                          int64_t k_row_stride, int q_head_stride, int k_head_stride,
+                          int n_q_heads, int n_kv_heads, int head_dim, int rot_dim,
+                          const float* q_weight, const float* k_weight,
+                          const int32_t* positions, int64_t rows, float theta, float eps,
+                          void* stream);
+
+/* The single-position form with caller-supplied cos/sin rows, exactly
+ * apply_rope_cached (core/cpu_ops.h:25-28) on fp32 device data.  When
+ * cos_row or sin_row is NULL, cos/sin are computed in registers (half-split
+ * layout, the layout of the fast path). */
+ANE_CUDA_API int ane_cuda_apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads,
+                               int head_dim, int q_head_stride, int k_head_stride,
+                               int rot_dim, int pos, float theta, const float* cos_row,
+                               const float* sin_row, void* stream);
+
+/* ---- SiLU-gated activation ---------------------------------------------
+ * out = silu(gate) * up with silu(x) = x / (1 + exp(-x)): silu_vec_inplace
+ * (core/cpu_ops.cpp:7-14) times up, the gate*sigmoid(gate)*up of the fused
+ * FFN (core/ane_runtime.cpp:393-395) in fp32 arithmetic.  out may alias
+ * gate or up. */
+ANE_CUDA_API int ane_cuda_silu_mul(int dtype, void* out, int64_t out_stride, const void* gate,
+                      int64_t gate_stride, const void* up, int64_t up_stride, int64_t rows,
+                      int n, void* stream);
+
+/* silu_vec_inplace (core/cpu_ops.cpp:7-14): x = x / (1 + exp(-x)). */
+ANE_CUDA_API int ane_cuda_silu_inplace(int dtype, void* x, int64_t n, void* stream);
+
+/* mul_sigmoid_inplace (core/cpu_ops.cpp:16-23): y = y / (1 + exp(-z)). */
+ANE_CUDA_API int ane_cuda_mul_sigmoid_inplace(int dtype, void* y, const void* z, int64_t n, void* stream);
+
+/* ---- softmax ------------------------------------------------------------
+ * softmax (core/cpu_ops.cpp:83-99), in place on fp32 rows: max, subtract,
+ * exp, sum, multiply by 1/sum. */
+ANE_CUDA_API int ane_cuda_softmax_rows(float* x, int64_t rows, int n, int64_t stride, void* stream);
+
+/* ---- sampler -------------------------------------------------------------
+ * sample_token (core/sampling.cpp:10-66) for a batch of rows.  For row r:
+ * the last `repetition_context` ids of history[r, 0:history_len[r]] (ids
+ * outside [0, vocab) ignored) give a count per distinct id; each such id's
+ * logit gets the repetition penalty (x > 0 ? x / p : x * p, when p > 1) and
+ * then x -= frequency_penalty * count (when > 0).  temperature <= 0: argmax
+ * (first maximum).  Otherwise x *= 1/temperature, softmax, and the result
+ * is the first i whose running fp32 sum of probabilities is >= uniforms[r]
+ * (vocab - 1 if none).  uniforms[r] plays the part of (float)drand48()
+ * (:58).  history / history_len may be NULL (no penalties).  Token ids are
+ * bit-exact given the same logits and uniforms. */
+ANE_CUDA_API int ane_cuda_sample_rows(const float* logits, int64_t rows, int vocab, int64_t logits_stride,
+                         const int32_t* history, const int32_t* history_len,
+                         int64_t history_stride, const float* uniforms, float temperature,
+                         float repetition_penalty, int repetition_context,
+                         float frequency_penalty, int32_t* out_tokens, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ANE_CUDA_H */

@@ -1,0 +1,439 @@
+/*
+ * oracle.c -- CPU restatement of ANE-LM's layer-op / sampler / convert path.
+ *
+ * TEST INFRASTRUCTURE ONLY (the checker, never the thing measured or
+ * shipped).  See oracle.h for the pinned definitions of what the reference
+ * leaves to Apple Accelerate.  Compile with -ffp-contract=off so that every
+ * multiply and add rounds on its own, exactly like the reference's vDSP
+ * element-wise calls and like the CUDA kernels' explicit __f*_rn intrinsics.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ */
+/* bit helpers                                                         */
+/* ------------------------------------------------------------------ */
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* ------------------------------------------------------------------ */
+/* Conversions                                                         */
+/* ------------------------------------------------------------------ */
+
+/* BF16 -> FP16 through FP32 with the reference's TRUNCATING f32_to_f16:
+ * include/ane_lm/common.h:21-26 (bf16_to_f32), :58-71 (f32_to_f16),
+ * :73-75 (bf16_to_f16).  Exponent re-bias by -112; exponent >= 31 (this
+ * includes Inf and NaN) saturates to signed Inf; exponent <= 0 shifts the
+ * mantissa (with its hidden bit) right and drops the low bits; below
+ * 2^-25 the result is a signed zero. */
+uint16_t or_bf16_to_f16(uint16_t bf) {
+    uint32_t bits = (uint32_t)bf << 16;
+    uint16_t sign = (uint16_t)((bits >> 16) & 0x8000u);
+    int32_t e = (int32_t)((bits >> 23) & 0xFFu) - 112;
+    uint32_t frac = bits & 0x7FFFFFu;
+    if (e <= 0) {
+        if (e < -10) return sign;
+        return (uint16_t)(sign | (uint16_t)((((frac | 0x800000u) >> (1 - e)) >> 13)));
+    }
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    return (uint16_t)(sign | (uint16_t)(e << 10) | (uint16_t)(frac >> 13));
+}
+
+/* include/ane_lm/common.h:81-83 */
+void or_bf16_to_f16_vec(uint16_t* out, const uint16_t* in, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = or_bf16_to_f16(in[i]);
+}
+
+/* Round-to-nearest-even FP32 -> FP16, the rounding of a native __fp16 store
+ * on arm64 (core/ane_runtime.cpp:604-609, :624), used for activations. */
+uint16_t or_f32_to_f16_rne(float f) {
+    uint32_t u = f2u(f);
+    uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    uint32_t a = u & 0x7FFFFFFFu;
+    if (a > 0x7F800000u) return (uint16_t)(sign | 0x7E00u);      /* NaN */
+    if (a >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);     /* >= 65520 */
+    if (a < 0x38800000u) {                                        /* < 2^-14 */
+        if (a < 0x33000000u) return sign;                         /* <= 2^-25 */
+        uint32_t e = a >> 23;
+        uint32_t m = (a & 0x7FFFFFu) | 0x800000u;
+        uint32_t sh = 126u - e;                                   /* 14..24 */
+        uint32_t q = m >> sh;
+        uint32_t rem = m & ((1u << sh) - 1u);
+        uint32_t half = 1u << (sh - 1u);
+        if (rem > half || (rem == half && (q & 1u))) q++;
+        return (uint16_t)(sign | q);
+    }
+    uint32_t e16 = (a >> 23) - 112u;
+    uint32_t q = (e16 << 10) | ((a & 0x7FFFFFu) >> 13);
+    uint32_t rem = a & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) q++;
+    return (uint16_t)(sign | q);
+}
+
+uint16_t or_f32_to_bf16_rne(float f) {
+    uint32_t u = f2u(f);
+    if ((u & 0x7FFFFFFFu) > 0x7F800000u) return (uint16_t)((u >> 16) | 0x40u);
+    uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7FFFu + lsb;
+    return (uint16_t)(u >> 16);
+}
+
+/* include/ane_lm/common.h:35-56 (exact widening) */
+float or_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1Fu;
+    uint32_t m = h & 0x3FFu;
+    if (e == 0) {
+        float v = (float)m * (1.0f / 16777216.0f);                /* m * 2^-24, exact */
+        return sign ? -v : v;
+    }
+    if (e == 31) return u2f(sign | 0x7F800000u | (m << 13));
+    return u2f(sign | ((e + 112u) << 23) | (m << 13));
+}
+
+float or_bf16_to_f32(uint16_t h) { return u2f((uint32_t)h << 16); }
+
+/* ------------------------------------------------------------------ */
+/* Pinned math                                                         */
+/* ------------------------------------------------------------------ */
+
+/* exp for vvexpf (core/cpu_ops.cpp:11,20,90).  Method: Cody & Waite (1980)
+ * argument reduction x = k ln2 + r with k = rint(x log2 e) and ln 2 split
+ * into a float head and tail, then the Taylor series of e^r to degree 7 by
+ * Horner's rule, then scaling by 2^k with at most two exact-or-once-rounded
+ * multiplies.  Constants are ln 2 and 1/n! rounded to float. */
+#define EXP_LOG2E  1.44269502162933349609375f       /* 0x3fb8aa3b */
+#define EXP_LN2_HI 0.693147182464599609375f         /* 0x3f317218 */
+#define EXP_LN2_LO (-1.904654212125933608e-09f)     /* 0xb102e308 */
+#define INV_FACT3  0.16666667163372039794921875f
+#define INV_FACT4  0.041666667908430099487304688f
+#define INV_FACT5  0.0083333337679505348205566406f
+#define INV_FACT6  0.0013888889225199818611145020f
+#define INV_FACT7  0.00019841270113829523324966431f
+
+static inline float pow2i(int k) { return u2f((uint32_t)(k + 127) << 23); } /* k in [-126,127] */
+
+float or_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return u2f(0x7F800000u);
+    if (x < -104.0f) return 0.0f;
+    float k = rintf(x * EXP_LOG2E);
+    float r = fmaf(-k, EXP_LN2_HI, x);
+    r = fmaf(-k, EXP_LN2_LO, r);
+    float p = fmaf(INV_FACT7, r, INV_FACT6);
+    p = fmaf(p, r, INV_FACT5);
+    p = fmaf(p, r, INV_FACT4);
+    p = fmaf(p, r, INV_FACT3);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ki = (int)k;
+    if (ki > 127) return (p * 2.0f) * pow2i(127);
+    if (ki < -126) return (p * pow2i(ki + 64)) * pow2i(-64);
+    return p * pow2i(ki);
+}
+
+/* sin/cos for the RoPE table (cosf/sinf at models/llm/qwen3.cpp:214-215).
+ * Method: Cody-Waite reduction by pi/2 carried out in double (pi/2 as a
+ * double head plus tail, two fma), the reduced argument rounded to float,
+ * Taylor polynomials of sin (degree 9) and cos (degree 10) in float by
+ * Horner's rule with fmaf, then the quadrant rotation. */
+#define SC_TWO_OVER_PI 0x1.45f306dc9c883p-1
+#define SC_PIO2_HI     0x1.921fb54442d18p+0
+#define SC_PIO2_LO     0x1.1a62633145c07p-54
+#define SIN_C1 (-0.16666667163372039794921875f)
+#define SIN_C2   0.0083333337679505348205566406f
+#define SIN_C3 (-0.00019841270113829523324966431f)
+#define SIN_C4   2.7557318844628753e-06f
+#define COS_C1 (-0.5f)
+#define COS_C2   0.041666667908430099487304688f
+#define COS_C3 (-0.0013888889225199818611145020f)
+#define COS_C4   2.4801587642286904e-05f
+#define COS_C5 (-2.755731998149713e-07f)
+
+void or_sincosf(float x, float* s, float* c) {
+    double xd = (double)x;
+    double kd = rint(xd * SC_TWO_OVER_PI);
+    double rd = fma(-kd, SC_PIO2_HI, xd);
+    rd = fma(-kd, SC_PIO2_LO, rd);
+    float r = (float)rd;
+    int q = (int)(kd - 4.0 * floor(kd * 0.25));
+    float r2 = r * r;
+    float t = fmaf(SIN_C4, r2, SIN_C3);
+    t = fmaf(t, r2, SIN_C2);
+    t = fmaf(t, r2, SIN_C1);
+    t = t * r2;
+    float sp = fmaf(t, r, r);
+    float u = fmaf(COS_C5, r2, COS_C4);
+    u = fmaf(u, r2, COS_C3);
+    u = fmaf(u, r2, COS_C2);
+    u = fmaf(u, r2, COS_C1);
+    float cp = fmaf(u, r2, 1.0f);
+    switch (q) {
+        case 0:  *s = sp;  *c = cp;  break;
+        case 1:  *s = cp;  *c = -sp; break;
+        case 2:  *s = -sp; *c = -cp; break;
+        default: *s = -cp; *c = sp;  break;
+    }
+}
+
+/* inv_freq table of models/llm/qwen3.cpp:205-208:
+ * inv_freq[j] = 1.0f / powf(theta, (float)(2j) / (float)rot_dim),
+ * with powf taken as the float rounding of the double pow. */
+void or_rope_inv_freq(float* inv_freq, int rot_dim, float theta) {
+    for (int j = 0; 2 * j < rot_dim; j++) {
+        float e = (float)(2 * j) / (float)rot_dim;
+        float p = (float)pow((double)theta, (double)e);
+        inv_freq[j] = 1.0f / p;
+    }
+}
+
+/* vDSP_svesq of core/cpu_ops.cpp:27 with the pinned 32-lane order. */
+float or_sumsq(const float* x, int dim, int vec) {
+    float acc[32];
+    for (int l = 0; l < 32; l++) acc[l] = 0.0f;
+    int nchunk = (dim + vec - 1) / vec;
+    for (int ch = 0; ch < nchunk; ch++) {
+        int l = ch & 31;
+        int end = (ch + 1) * vec < dim ? (ch + 1) * vec : dim;
+        for (int e = ch * vec; e < end; e++) acc[l] = fmaf(x[e], x[e], acc[l]);
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        float nx[32];
+        for (int l = 0; l < 32; l++) nx[l] = acc[l] + acc[l ^ off];
+        memcpy(acc, nx, sizeof(acc));
+    }
+    return acc[0];
+}
+
+/* vDSP_sve of core/cpu_ops.cpp:92 with the pinned 1024-thread order. */
+float or_softmax_sum(const float* e, int n) {
+    static const int T = 1024;
+    float acc[1024];
+    for (int t = 0; t < T; t++) acc[t] = 0.0f;
+    for (int i = 0; i < n; i++) {
+        int t = (i >> 2) & (T - 1);
+        acc[t] = acc[t] + e[i];
+    }
+    float w[32];
+    for (int g = 0; g < 32; g++) {
+        float* a = acc + 32 * g;
+        for (int off = 16; off >= 1; off >>= 1) {
+            float nx[32];
+            for (int l = 0; l < 32; l++) nx[l] = a[l] + a[l ^ off];
+            memcpy(a, nx, sizeof(nx));
+        }
+        w[g] = a[0];
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        float nx[32];
+        for (int l = 0; l < 32; l++) nx[l] = w[l] + w[l ^ off];
+        memcpy(w, nx, sizeof(nx));
+    }
+    return w[0];
+}
+
+/* ------------------------------------------------------------------ */
+/* element access by dtype                                             */
+/* ------------------------------------------------------------------ */
+static inline float ld(const void* p, int dt, int64_t i) {
+    if (dt == OR_F32) return ((const float*)p)[i];
+    if (dt == OR_F16) return or_f16_to_f32(((const uint16_t*)p)[i]);
+    return or_bf16_to_f32(((const uint16_t*)p)[i]);
+}
+static inline void st(void* p, int dt, int64_t i, float v) {
+    if (dt == OR_F32) ((float*)p)[i] = v;
+    else if (dt == OR_F16) ((uint16_t*)p)[i] = or_f32_to_f16_rne(v);
+    else ((uint16_t*)p)[i] = or_f32_to_bf16_rne(v);
+}
+static inline int vec_of(int dt) { return dt == OR_F32 ? 4 : 8; }
+
+/* rmsnorm, core/cpu_ops.cpp:25-31:
+ *   inv = 1 / sqrtf(sumsq / dim + eps); out = (x * inv) * w   (two roundings)
+ * preceded, when d is given, by the residual add of models/llm/qwen3.cpp:516
+ * and :527 (x += d).  The sum is stored back into x in x's dtype and the
+ * norm reads the stored value, as an unfused add-then-norm would. */
+void or_residual_rmsnorm(int dt, void* x, int64_t xs, const void* d, int64_t ds,
+                         void* out, int64_t os, const float* w,
+                         int64_t rows, int dim, float eps) {
+    float* v = (float*)malloc((size_t)dim * sizeof(float));
+    for (int64_t r = 0; r < rows; r++) {
+        for (int i = 0; i < dim; i++) {
+            float xv = ld(x, dt, r * xs + i);
+            if (d) {
+                float s = xv + ld(d, dt, r * ds + i);
+                st(x, dt, r * xs + i, s);
+                xv = ld(x, dt, r * xs + i);
+            }
+            v[i] = xv;
+        }
+        float ss = or_sumsq(v, dim, vec_of(dt));
+        float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+        for (int i = 0; i < dim; i++) {
+            float y = v[i] * inv;
+            y = y * w[i];
+            st(out, dt, r * os + i, y);
+        }
+    }
+    free(v);
+}
+
+/* Per-head QK-norm (models/llm/qwen3.cpp:444-461, rmsnorm of each head with
+ * q_norm / k_norm) followed by half-split RoPE (core/cpu_ops.cpp:43-54,
+ * :56-66; models/llm/qwen3.cpp:17-52):
+ *   v[j]      = v[j] * cos - v[j+half] * sin
+ *   v[j+half] = v[j+half] * cos + v[j] * sin        (unfused, as vmmsb/vmma)
+ * with half = rot_dim / 2; elements past rot_dim are only normalised. */
+void or_qk_norm_rope(int dt, void* q, void* k, int64_t qrs, int64_t krs,
+                     int qhs, int khs, int nq, int nkv, int hd, int rot,
+                     const float* qw, const float* kw, const int32_t* pos,
+                     int64_t rows, float theta, float eps) {
+    int half = rot / 2;
+    float* inv_freq = (float*)malloc((size_t)(half > 0 ? half : 1) * sizeof(float));
+    float* cs = (float*)malloc((size_t)(half > 0 ? half : 1) * sizeof(float));
+    float* sn = (float*)malloc((size_t)(half > 0 ? half : 1) * sizeof(float));
+    float* v = (float*)malloc((size_t)hd * sizeof(float));
+    or_rope_inv_freq(inv_freq, rot, theta);
+    for (int64_t r = 0; r < rows; r++) {
+        float fp = (float)pos[r];
+        for (int j = 0; j < half; j++) or_sincosf(fp * inv_freq[j], &sn[j], &cs[j]);
+        for (int h = 0; h < nq + nkv; h++) {
+            void* base = h < nq ? q : k;
+            int64_t off = h < nq ? r * qrs + (int64_t)h * qhs
+                                 : r * krs + (int64_t)(h - nq) * khs;
+            const float* w = h < nq ? qw : kw;
+            for (int i = 0; i < hd; i++) v[i] = ld(base, dt, off + i);
+            float ss = or_sumsq(v, hd, vec_of(dt));
+            float inv = 1.0f / sqrtf(ss / (float)hd + eps);
+            for (int i = 0; i < hd; i++) { float y = v[i] * inv; v[i] = y * w[i]; }
+            for (int j = 0; j < half; j++) {
+                float a = v[j], b = v[j + half];
+                float ac = a * cs[j], bs = b * sn[j];
+                float bc = b * cs[j], as = a * sn[j];
+                v[j] = ac - bs;
+                v[j + half] = bc + as;
+            }
+            for (int i = 0; i < hd; i++) st(base, dt, off + i, v[i]);
+        }
+    }
+    free(inv_freq); free(cs); free(sn); free(v);
+}
+
+/* SiLU-gated activation: silu_vec_inplace (core/cpu_ops.cpp:7-14,
+ * x / (1 + exp(-x))) times up, the gate*sigmoid(gate)*up of the fused FFN
+ * (core/ane_runtime.cpp:393-395) evaluated in fp32. */
+void or_silu_mul(int dt, void* out, int64_t os, const void* g, int64_t gs,
+                 const void* u, int64_t us, int64_t rows, int n) {
+    for (int64_t r = 0; r < rows; r++) {
+        for (int i = 0; i < n; i++) {
+            float gv = ld(g, dt, r * gs + i);
+            float den = 1.0f + or_expf(-gv);
+            float s = gv / den;
+            float h = s * ld(u, dt, r * us + i);
+            st(out, dt, r * os + i, h);
+        }
+    }
+}
+
+/* Embedding gather, models/llm/qwen3.cpp:498 (memcpy of row token*hidden),
+ * batched.  Rows whose id is outside [0, vocab) are written as zeros and
+ * counted.  out_dtype is the table's dtype (byte copy) or F32 from an
+ * F16/BF16 table (exact widening). */
+int64_t or_embedding_gather(void* out, int odt, const void* table, int tdt,
+                            const int32_t* ids, int64_t rows, int vocab, int hidden) {
+    int64_t bad = 0;
+    size_t tes = tdt == OR_F32 ? 4 : 2, oes = odt == OR_F32 ? 4 : 2;
+    for (int64_t r = 0; r < rows; r++) {
+        int32_t id = ids[r];
+        char* o = (char*)out + (size_t)r * hidden * oes;
+        if (id < 0 || id >= vocab) { memset(o, 0, (size_t)hidden * oes); bad++; continue; }
+        const char* t = (const char*)table + (size_t)id * hidden * tes;
+        if (odt == tdt) memcpy(o, t, (size_t)hidden * tes);
+        else for (int i = 0; i < hidden; i++) ((float*)o)[i] = ld(t, tdt, i);
+    }
+    return bad;
+}
+
+/* softmax, core/cpu_ops.cpp:83-99, in place over rows:
+ * max (vDSP_maxv), x + (-max) (vDSP_vsadd), exp (vvexpf), sum (vDSP_sve,
+ * pinned order), x * (1 / sum) (vDSP_vsmul). */
+void or_softmax_rows(float* x, int64_t rows, int n, int64_t stride) {
+    for (int64_t r = 0; r < rows; r++) {
+        float* v = x + r * stride;
+        float mx = v[0];
+        for (int i = 1; i < n; i++) if (v[i] > mx) mx = v[i];
+        float nmx = -mx;
+        for (int i = 0; i < n; i++) v[i] = or_expf(v[i] + nmx);
+        float inv = 1.0f / or_softmax_sum(v, n);
+        for (int i = 0; i < n; i++) v[i] *= inv;
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* Sampler, core/sampling.cpp:10-66 and softmax core/cpu_ops.cpp:83-99  */
+/* ------------------------------------------------------------------ */
+static int32_t sample_one(const float* logits, int vocab, const int32_t* hist,
+                          int hl, float u, float temperature, float rep,
+                          int ctx, float freq, float* adj, int32_t* cnt,
+                          int32_t* uniq) {
+    memcpy(adj, logits, (size_t)vocab * sizeof(float));
+    if (hl > 0) {
+        /* window = last `ctx` ids (sampling.cpp:17), ids outside the vocab
+         * are ignored (:22) */
+        int start = hl - ctx;
+        if (start < 0) start = 0;
+        int nu = 0;
+        for (int j = start; j < hl; j++) {
+            int32_t t = hist[j];
+            if (t >= 0 && t < vocab) {
+                if (cnt[t] == 0) uniq[nu++] = t;
+                cnt[t]++;
+            }
+        }
+        /* per distinct id: repetition penalty then frequency penalty (:29-42) */
+        for (int i = 0; i < nu; i++) {
+            int32_t t = uniq[i];
+            if (rep > 1.0f) adj[t] = adj[t] > 0.0f ? adj[t] / rep : adj[t] * rep;
+            if (freq > 0.0f) adj[t] -= freq * (float)cnt[t];
+            cnt[t] = 0;
+        }
+    }
+    if (temperature <= 0.0f) {                                    /* :45-52 */
+        int mi = 0;
+        for (int i = 1; i < vocab; i++) if (adj[i] > adj[mi]) mi = i;
+        return mi;
+    }
+    float inv_t = 1.0f / temperature;                             /* :54-55 */
+    for (int i = 0; i < vocab; i++) adj[i] *= inv_t;
+    float mx = adj[0];                                            /* softmax */
+    for (int i = 1; i < vocab; i++) if (adj[i] > mx) mx = adj[i];
+    float nmx = -mx;
+    for (int i = 0; i < vocab; i++) adj[i] = or_expf(adj[i] + nmx);
+    float sum = or_softmax_sum(adj, vocab);
+    float inv = 1.0f / sum;
+    for (int i = 0; i < vocab; i++) adj[i] *= inv;
+    float cum = 0.0f;                                             /* :58-65 */
+    for (int i = 0; i < vocab; i++) {
+        cum += adj[i];
+        if (cum >= u) return i;
+    }
+    return vocab - 1;
+}
+
+void or_sample_rows(const float* logits, int64_t rows, int vocab, int64_t ls,
+                    const int32_t* history, const int32_t* history_len,
+                    int64_t hs, const float* uniforms, float temperature,
+                    float rep, int ctx, float freq, int32_t* out) {
+    float* adj = (float*)malloc((size_t)vocab * sizeof(float));
+    int32_t* cnt = (int32_t*)calloc((size_t)vocab, sizeof(int32_t));
+    int32_t* uniq = (int32_t*)malloc((size_t)(hs > 0 ? hs : 1) * sizeof(int32_t));
+    for (int64_t r = 0; r < rows; r++) {
+        int hl = history_len ? history_len[r] : 0;
+        out[r] = sample_one(logits + r * ls, vocab, history ? history + r * hs : NULL,
+                            hl, uniforms[r], temperature, rep, ctx, freq, adj, cnt, uniq);
+    }
+    free(adj); free(cnt); free(uniq);
+}

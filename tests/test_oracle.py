@@ -1,0 +1,199 @@
+"""CPU tests of the oracle: the C restatement (oracle/oracle.c) against the
+reference's own code compiled with the shim (oracle/_ref) and against the
+committed golden fixtures that reference build produced."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+from oracle_lib import F16, f16_ulp_diff, f32_ulp_diff
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def gold(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def ptr(a):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+# ---------------------------------------------------------------- convert
+def test_bf16_to_f16_golden_exhaustive(oracle):
+    g = gold("bf16_to_f16.npz")
+    assert np.array_equal(oracle.bf16_to_f16(g["bf16"]), g["f16"])
+
+
+def test_bf16_to_f16_known_answers(oracle):
+    # include/ane_lm/common.h:58-71 truncates and saturates NaN/overflow to Inf
+    cases = {0x3F80: 0x3C00, 0x4780: 0x7C00, 0x7FC0: 0x7C00, 0x33C0: 0x0001, 0xFF80: 0xFC00,
+             0x0000: 0x0000, 0x8000: 0x8000, 0x477F: 0x7BF8, 0x3380: 0x0001, 0x3300: 0x0000,
+             0xC780: 0xFC00, 0x0001: 0x0000}
+    inp = np.array(list(cases), np.uint16)
+    got = oracle.bf16_to_f16(inp)
+    assert [hex(v) for v in got] == [hex(v) for v in cases.values()]
+
+
+# ---------------------------------------------------------------- pinned math
+def test_expf_accuracy(oracle):
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.uniform(-104, 88.7, 100000), rng.uniform(-1, 1, 20000),
+                        [0.0, -0.0, 1.0, -1.0, 88.7, -87.3]]).astype(np.float32)
+    e = oracle.expf(x)
+    t = np.exp(x.astype(np.float64)).astype(np.float32)
+    normal = t > np.float32(1.2e-38)
+    assert f32_ulp_diff(e[normal], t[normal]).max() <= 1
+    assert np.all(np.abs(e[~normal] - t[~normal]) <= np.float32(2 ** -149))
+    assert oracle.expf(np.array([0.0], np.float32))[0] == 1.0
+    assert oracle.expf(np.array([-105.0], np.float32))[0] == 0.0
+    assert np.isinf(oracle.expf(np.array([89.0], np.float32))[0])
+
+
+def test_sincos_accuracy(oracle):
+    rng = np.random.default_rng(4)
+    xs = np.concatenate([rng.uniform(0, 4096, 5000), rng.uniform(0, 2e5, 2000),
+                         [0.0, 1e-8, np.pi / 4, np.pi / 2, 100000.0]]).astype(np.float32)
+    worst = 0
+    for v in xs:
+        s, c = oracle.sincosf(v)
+        ts = np.float32(np.sin(np.float64(v)))
+        tc = np.float32(np.cos(np.float64(v)))
+        # absolute error relative to 1 ulp at magnitude 1 keeps near-zero values fair
+        worst = max(worst, abs(s - ts) / 2 ** -24, abs(c - tc) / 2 ** -24)
+    assert worst <= 2.0
+
+
+def test_rope_inv_freq_matches_model_table(oracle, ref):
+    # models/llm/qwen3.cpp:205-208 with libm powf vs the oracle's rounded double pow
+    inv = oracle.rope_inv_freq(128, 1e6)
+    cos = np.empty(64, np.float32)
+    sin = np.empty(64, np.float32)
+    ref.ref_rope_row(ptr(cos), ptr(sin), 1, 128, np.float32(1e6))
+    # at pos = 1 the reference's angle is exactly inv_freq
+    for j in range(64):
+        s, c = oracle.sincosf(inv[j])
+        assert abs(c - cos[j]) <= 2 ** -23 and abs(s - sin[j]) <= 2 ** -23
+
+
+# ---------------------------------------------------------------- rmsnorm
+def test_rmsnorm_f32_golden(oracle):
+    g = gold("rmsnorm.npz")
+    for dim in (128, 1024, 2048, 4096, 1000):
+        x, w, y = g[f"x_{dim}"], g[f"w_{dim}"], g[f"y_{dim}"]
+        _, got = oracle.residual_rmsnorm(x, None, w)
+        # the shim's vDSP_svesq is the pinned 32-lane order over 4-float chunks,
+        # so the fp32 restatement is bit-exact with the reference routine
+        assert np.array_equal(got, y), dim
+
+
+def test_rmsnorm_f16_vs_reference(oracle, ref):
+    rng = np.random.default_rng(5)
+    for dim in (1024, 2048, 4096):
+        x = rng.standard_normal((8, dim)).astype(np.float16)
+        d = rng.standard_normal((8, dim)).astype(np.float16)
+        w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+        xo, yo = oracle.residual_rmsnorm(x, d, w)
+        xs = (x.astype(np.float32) + d.astype(np.float32)).astype(np.float16)
+        assert np.array_equal(xo, xs)
+        yr = np.empty((8, dim), np.float32)
+        xf = xs.astype(np.float32)
+        for r in range(8):
+            ref.ref_rmsnorm(ptr(yr[r]), ptr(xf[r]), ptr(w), dim, np.float32(1e-6))
+        assert f16_ulp_diff(yo, yr.astype(np.float16)).max() <= 1
+
+
+# ---------------------------------------------------------------- QK-norm + RoPE
+def test_qk_norm_rope_golden(oracle):
+    g = gold("qk_rope.npz")
+    nq, nkv, hd = (int(v) for v in g["shape"])
+    qk_in = g["qk_in"]
+    rows = qk_in.shape[0]
+    qkv = np.concatenate([qk_in.reshape(rows, -1), np.zeros((rows, nkv * hd), np.float32)], 1)
+    got = oracle.qk_norm_rope(qkv, nq, nkv, hd, g["qw"], g["kw"], g["positions"],
+                              float(g["theta"]))
+    got = got[:, :(nq + nkv) * hd].reshape(qk_in.shape)
+    want = g["qk_out"]
+    # the reference table uses libm cosf/sinf, the oracle its pinned sin/cos;
+    # both are within ~1 ulp of the true values
+    scale = np.maximum(np.abs(want), 1.0)
+    assert np.max(np.abs(got - want) / scale) < 2e-6
+    assert f16_ulp_diff(got.astype(np.float16), want.astype(np.float16)).max() <= 1
+
+
+# ---------------------------------------------------------------- SiLU
+def test_silu_golden(oracle):
+    g = gold("silu.npz")
+    x = g["x"][None, :]
+    got = oracle.silu_mul(x, np.ones_like(x))[0]
+    # vvexpf is the pinned exp in both: bit-exact
+    assert np.array_equal(got.view(np.int32), g["y"].view(np.int32))
+
+
+# ---------------------------------------------------------------- sampler
+def test_sampler_golden(oracle):
+    g = gold("sampler.npz")
+    for i in range(g["tokens"].size):
+        tok = oracle.sample_rows(g["logits"][i:i + 1], g["uniforms"][i:i + 1],
+                                 g["history"][i:i + 1], g["history_len"][i:i + 1],
+                                 temperature=float(g["temperature"][i]), rep=float(g["rep"][i]))
+        assert tok[0] == g["tokens"][i], i
+
+
+@pytest.mark.parametrize("vocab", [7, 1000, 151936])
+def test_sampler_vs_reference(oracle, ref, vocab):
+    rng = np.random.default_rng(vocab)
+    n = 6 if vocab > 100000 else 40
+    for i in range(n):
+        lg = (rng.standard_normal(vocab) * 3).astype(np.float32)
+        hl = int(rng.integers(0, 1100))
+        hist = rng.integers(-2, vocab + 2, size=max(hl, 1)).astype(np.int32)
+        temp = [0.6, 0.0, 1.3, -1.0][i % 4]
+        u = C.c_float()
+        want = ref.ref_sample_token(ptr(lg), vocab, np.float32(temp), np.float32(1.2), 256,
+                                    np.float32(0.1), ptr(hist), hl, 77 + i, C.byref(u))
+        got = oracle.sample_rows(lg[None], np.array([u.value], np.float32), hist[None],
+                                 np.array([hl], np.int32), temperature=temp)
+        assert got[0] == want, (i, temp, hl)
+
+
+# ---------------------------------------------------------------- gather
+def test_gather(oracle):
+    rng = np.random.default_rng(9)
+    table = rng.standard_normal((100, 64)).astype(np.float16)
+    ids = np.array([0, 99, 5, -1, 100, 42], np.int32)
+    out, bad = oracle.embedding_gather(table, ids)
+    assert bad == 2
+    assert np.array_equal(out[[0, 1, 2, 5]], table[[0, 99, 5, 42]])
+    assert not out[[3, 4]].any()
+    out32, _ = oracle.embedding_gather(table, ids, out_dtype=0)
+    assert np.array_equal(out32[0], table[0].astype(np.float32))
+
+
+# ---------------------------------------------------------------- whole chain
+def test_layer_chain_f16_vs_reference(oracle, ref):
+    rng = np.random.default_rng(11)
+    rows, hidden, nq, nkv, hd, inter = 6, 512, 4, 2, 128, 768
+    x = rng.standard_normal((rows, hidden)).astype(np.float16)
+    d = rng.standard_normal((rows, hidden)).astype(np.float16)
+    w = (1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    qkv = rng.standard_normal((rows, (nq + 2 * nkv) * hd)).astype(np.float16)
+    qw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    pos = np.array([0, 1, 5, 511, 2047, 9000], np.int32)
+    g = rng.standard_normal((rows, inter)).astype(np.float16)
+    u = rng.standard_normal((rows, inter)).astype(np.float16)
+    g[0, :5] *= 50
+
+    xr, yr, qr, hr = x.copy(), np.empty_like(x), qkv.copy(), np.empty_like(g)
+    ref.ref_layer_chain_f16(ptr(xr), ptr(d), ptr(yr), ptr(w), ptr(qr), ptr(qw), ptr(kw), ptr(pos),
+                            ptr(g), ptr(u), ptr(hr), 0, rows, hidden, nq, nkv, hd, inter,
+                            np.float32(1e6), np.float32(1e-6))
+    xo, yo = oracle.residual_rmsnorm(x, d, w)
+    qo = oracle.qk_norm_rope(qkv, nq, nkv, hd, qw, kw, pos, 1e6)
+    ho = oracle.silu_mul(g, u)
+    assert np.array_equal(xo, xr)
+    assert f16_ulp_diff(yo, yr).max() <= 2
+    assert f16_ulp_diff(qo, qr).max() <= 2
+    assert f16_ulp_diff(ho, hr).max() <= 2
