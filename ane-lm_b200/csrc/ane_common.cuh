@@ -101,6 +101,19 @@ __device__ __forceinline__ float pinned_expf(float x) {
     return __fmul_rn(p, pow2i(ki));
 }
 
+// 2^x and 1/x from the special-function unit (ex2.approx.ftz, rcp.approx.ftz):
+// a few ulp of fp32, used only where the result is rounded to 16 bits.
+__device__ __forceinline__ float exp2f_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // ---------------------------------------------------------------------
 // sin / cos for RoPE: reduction by pi/2 in double (pi/2 as double head +
 // tail, two fma), reduced argument rounded to float, Taylor polynomials of
@@ -130,6 +143,56 @@ __device__ __forceinline__ void pinned_sincosf(float x, float* s, float* c) {
         case 2:  *s = -sp; *c = -cp; break;
         default: *s = -cp; *c = sp;  break;
     }
+}
+
+// ---------------------------------------------------------------------
+// Bulk async copies (TMA engine, no tensor map) and mbarriers.  Loads are
+// plain per-CTA copies: no cluster multicast anywhere in this library.
+// ---------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes) : "memory");
+}
+// global -> shared, `bytes` a multiple of 16, both addresses 16-byte aligned
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// orders this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (bulk copy) accesses
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return ok != 0;
+}
+// Waits for `phase` of `bar` for at most ~2^32 SM clock cycles (about 2 s);
+// false on timeout.  Every wait in this library is bounded.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, phase)) {
+        if (clock64() - t0 > (1ll << 32)) return false;
+    }
+    return true;
 }
 
 // Lane-partial fmaf chain of the pinned sum of squares (one chunk).

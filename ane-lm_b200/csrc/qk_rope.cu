@@ -2,17 +2,19 @@
 // (models/llm/qwen3.cpp:444-473; core/cpu_ops.cpp:43-80).
 //
 // Fast path (rot_dim == head_dim, head_dim / kVec a power of two in
-// [2, 32], 16-byte aligned rows): one warp per row.  A head is served by
+// [2, 32], 16-byte aligned rows): one warp per unit of about 8 heads of a
+// row.  A head is served by
 // GL = chunks/2 lanes; lane l of the group holds chunk l (elements
 // [l*V, l*V+V), first half) and chunk l + GL (the RoPE partners j + half).
 // With that layout
 //   - the first butterfly stage of the pinned sum-of-squares order
 //     (offset GL) is an add inside the lane, the rest are xor shuffles
 //     inside the group; no shuffle is needed for RoPE;
-//   - the lane's cos/sin for j in [l*V, l*V+V) serve every head of the row,
-//     so they are computed once per row, in registers.
-// The whole row (all q and k heads) is loaded before any math so that each
-// warp keeps NIT*2 16-byte loads in flight.
+//   - the lane's cos/sin for j in [l*V, l*V+V) serve every head of the unit,
+//     so they are computed once per unit, in registers;
+//   - the lane's norm weights are the same for every q (k) head: loaded
+//     once per unit as 16-byte vectors.
+// All of the unit's heads are loaded before any math.
 //
 // Generic path (partial RoPE, other head sizes, unaligned rows, or the
 // caller-supplied cos/sin rows of apply_rope_cached): one warp per
@@ -45,46 +47,78 @@ struct QkArgs {
     const float* sin_row;
 };
 
-template <typename T, int NIT>
-__global__ void __launch_bounds__(kQkWarps * kWarp)
-qk_norm_rope_fast_kernel(const QkArgs a, const RopeFreq fr, const int gl_log2) {
+// A work unit is IPU head iterations (IPU * hpw heads) of one row; one
+// warp per unit, 8 warps per CTA.  Small units keep the register footprint
+// low (many warps per SM hide the load latency) while every unit still
+// moves 2 KB or more with 16-byte accesses.
+constexpr int kUnitWarps = 8;
+
+template <typename T, int IPU>
+__global__ void __launch_bounds__(kUnitWarps * kWarp)
+qk_norm_rope_unit_kernel(const QkArgs a, const RopeFreq fr, const int gl_log2,
+                         const int units_per_row, const bool pow2_dim) {
     using S = typename T::storage;
     constexpr int V = T::kVec;
     const int lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * kQkWarps + (threadIdx.x >> 5);
-    if (row >= a.rows) return;
+    const int64_t unit = (int64_t)blockIdx.x * kUnitWarps + (threadIdx.x >> 5);
+    if (unit >= a.rows * units_per_row) return;
+    const int64_t row = unit / units_per_row;
     const int GL = 1 << gl_log2;           // lanes per head
-    const int hpw = kWarp >> gl_log2;      // heads per warp iteration
+    const int hpw = kWarp >> gl_log2;      // heads per iteration
     const int g = lane >> gl_log2;         // head slot of this lane
     const int l = lane & (GL - 1);         // lane within the head group
     const int half = GL * V;               // rot_dim / 2
     const int nh = a.n_q + a.n_kv;
+    const int head0 = (int)(unit - row * units_per_row) * IPU * hpw;
     S* qrow = (S*)a.q + row * a.q_row_stride;
     S* krow = (S*)a.k + row * a.k_row_stride;
 
-    uint4 lo[NIT], hi[NIT];
+    uint4 lo[IPU], hi[IPU];
 #pragma unroll
-    for (int it = 0; it < NIT; it++) {
-        const int h = it * hpw + g;
+    for (int it = 0; it < IPU; it++) {
+        const int h = head0 + it * hpw + g;
         if (h < nh) {
-            S* base = h < a.n_q ? qrow + (int64_t)h * a.q_head_stride
-                                : krow + (int64_t)(h - a.n_q) * a.k_head_stride;
+            const S* base = h < a.n_q ? qrow + (int64_t)h * a.q_head_stride
+                                      : krow + (int64_t)(h - a.n_q) * a.k_head_stride;
             lo[it] = ld_stream(base + l * V);
             hi[it] = ld_stream(base + half + l * V);
         }
     }
 
-    // cos/sin of this lane's frequencies at the row's position
+    // cos/sin of the lane's V frequencies at the row's position.  The hpw
+    // lanes sharing l need the same values: each computes cpl of them and
+    // the rest arrive by shuffle.
     const float fpos = (float)(a.positions ? __ldg(a.positions + row) : a.pos);
+    const int cpl = half >= 32 ? half / 32 : V;
     float cs[V], sn[V];
+    if (cpl == V) {
 #pragma unroll
-    for (int e = 0; e < V; e++) pinned_sincosf(__fmul_rn(fpos, fr.f[l * V + e]), &sn[e], &cs[e]);
+        for (int e = 0; e < V; e++) pinned_sincosf(__fmul_rn(fpos, fr.f[l * V + e]), &sn[e], &cs[e]);
+    } else {
+        float mc[4], ms[4];
+#pragma unroll
+        for (int c = 0; c < 4; c++)
+            if (c < cpl) pinned_sincosf(__fmul_rn(fpos, fr.f[l * V + g * cpl + c]), &ms[c], &mc[c]);
+#pragma unroll
+        for (int e = 0; e < V; e++) {
+            const int src = (e / cpl) * GL + l;
+            float vc = mc[0], vs = ms[0];
+#pragma unroll
+            for (int c = 1; c < 4; c++)
+                if (e % cpl == c) { vc = mc[c]; vs = ms[c]; }
+            cs[e] = __shfl_sync(0xffffffffu, vc, src);
+            sn[e] = __shfl_sync(0xffffffffu, vs, src);
+        }
+    }
 
     const bool norm = a.qw != nullptr;
+    float w0[V], w1[V];
+    int wtype = -1;  // 0: q weights loaded, 1: k weights loaded
+    const float inv_dim = 1.0f / (float)a.head_dim;
 #pragma unroll
-    for (int it = 0; it < NIT; it++) {
-        if (it * hpw >= nh) break;  // warp-uniform
-        const int h = it * hpw + g;
+    for (int it = 0; it < IPU; it++) {
+        const int h = head0 + it * hpw + g;
+        if (head0 + it * hpw >= nh) break;  // warp-uniform
         const bool live = h < nh;
         float x0[V], x1[V];
         if (live) {
@@ -98,14 +132,25 @@ qk_norm_rope_fast_kernel(const QkArgs a, const RopeFreq fr, const int gl_log2) {
             float acc = __fadd_rn(sumsq_chain<V>(x0, 0.0f), sumsq_chain<V>(x1, 0.0f));
             for (int off = GL >> 1; off >= 1; off >>= 1)
                 acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-            const float inv = rms_inv(acc, a.head_dim, a.eps);
-            const float* w = h < a.n_q ? a.qw : a.kw;
-            if (live) {
+            // ss / dim is exact as a multiply when dim is a power of two
+            const float mean = pow2_dim ? __fmul_rn(acc, inv_dim) : __fdiv_rn(acc, (float)a.head_dim);
+            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+            const int want = h < a.n_q ? 0 : 1;
+            if (want != wtype) {
+                const float* wsrc = want == 0 ? a.qw : a.kw;
 #pragma unroll
-                for (int e = 0; e < V; e++) {
-                    x0[e] = __fmul_rn(__fmul_rn(x0[e], inv), __ldg(w + l * V + e));
-                    x1[e] = __fmul_rn(__fmul_rn(x1[e], inv), __ldg(w + half + l * V + e));
+                for (int q4 = 0; q4 < V / 4; q4++) {
+                    const float4 t0 = __ldg(reinterpret_cast<const float4*>(wsrc + l * V) + q4);
+                    const float4 t1 = __ldg(reinterpret_cast<const float4*>(wsrc + half + l * V) + q4);
+                    w0[4 * q4] = t0.x; w0[4 * q4 + 1] = t0.y; w0[4 * q4 + 2] = t0.z; w0[4 * q4 + 3] = t0.w;
+                    w1[4 * q4] = t1.x; w1[4 * q4 + 1] = t1.y; w1[4 * q4 + 2] = t1.z; w1[4 * q4 + 3] = t1.w;
                 }
+                wtype = want;
+            }
+#pragma unroll
+            for (int e = 0; e < V; e++) {
+                x0[e] = __fmul_rn(__fmul_rn(x0[e], inv), w0[e]);
+                x1[e] = __fmul_rn(__fmul_rn(x1[e], inv), w1[e]);
             }
         }
         if (live) {
@@ -205,18 +250,20 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s) {
                 gl_log2 >= 0 && nchunk <= 32 && is_aligned(a.q, 16) && is_aligned(a.k, 16) &&
                 (a.q_row_stride * es) % 16 == 0 && (a.k_row_stride * es) % 16 == 0 &&
                 (a.q_head_stride * es) % 16 == 0 && (a.k_head_stride * es) % 16 == 0;
-    const int hpw = fast ? kWarp >> gl_log2 : 1;
-    const int nit = (nh + hpw - 1) / hpw;
-    if (fast && nit <= 24) {
-        const unsigned blocks = (unsigned)((a.rows + kQkWarps - 1) / kQkWarps);
-#define ANE_QK_FAST(N) qk_norm_rope_fast_kernel<T, N><<<blocks, kQkWarps * kWarp, 0, s>>>(a, fr, gl_log2)
-        if (nit <= 2) ANE_QK_FAST(2);
-        else if (nit <= 4) ANE_QK_FAST(4);
-        else if (nit <= 8) ANE_QK_FAST(8);
-        else if (nit <= 12) ANE_QK_FAST(12);
-        else if (nit <= 16) ANE_QK_FAST(16);
-        else ANE_QK_FAST(24);
-#undef ANE_QK_FAST
+    if (fast && (!a.qw || (is_aligned(a.qw, 16) && is_aligned(a.kw, 16)))) {
+        const int hpw = kWarp >> gl_log2;
+        const int ipu = hpw >= 8 ? 1 : 8 / hpw;   // about 8 heads per unit
+        const int units_per_row = (nh + ipu * hpw - 1) / (ipu * hpw);
+        const int64_t units = a.rows * units_per_row;
+        const unsigned blocks = (unsigned)((units + kUnitWarps - 1) / kUnitWarps);
+        const bool pow2 = (a.head_dim & (a.head_dim - 1)) == 0;
+#define ANE_QK_UNIT(N) \
+    qk_norm_rope_unit_kernel<T, N><<<blocks, kUnitWarps * kWarp, 0, s>>>(a, fr, gl_log2, units_per_row, pow2)
+        if (ipu == 1) ANE_QK_UNIT(1);
+        else if (ipu == 2) ANE_QK_UNIT(2);
+        else if (ipu == 4) ANE_QK_UNIT(4);
+        else ANE_QK_UNIT(8);
+#undef ANE_QK_UNIT
     } else {
         if (a.head_dim > kGenericMaxHead)
             return fail(ANE_CUDA_ERR_UNSUPPORTED, "qk_norm_rope: head_dim %d > %d", a.head_dim,

@@ -6,9 +6,12 @@
 //   MUL_SIGMOID y   =  y / (1 + exp(-z))                 mul_sigmoid_inplace
 //
 // Element-wise and HBM-bound: 16-byte vectors, evict-first accesses, a grid
-// sized to the SM count.  exp is the pinned Cody-Waite/Taylor exp and the
-// divide is IEEE, each step rounded on its own, as the reference's vneg /
-// vvexpf / vsadd / vdiv sequence.
+// sized to the SM count.  fp32 rows use the pinned Cody-Waite/Taylor exp and
+// an IEEE divide, each step rounded on its own, as the reference's vneg /
+// vvexpf / vsadd / vdiv sequence (bit-exact).  fp16 / bf16 rows use the
+// special-function unit's exp2 and reciprocal: the pinned form costs about
+// 40 instructions per element, which at 6 bytes per element would make the
+// kernel issue-bound well below the HBM roofline.
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
@@ -16,8 +19,10 @@ namespace ane {
 
 enum ActMode { SILU_MUL = 0, SILU = 1, MUL_SIGMOID = 2 };
 
+// fp32 results: the pinned exp and an IEEE divide, bit-exact with the
+// reference's vneg / vvexpf / vsadd / vdiv sequence.
 template <int MODE>
-__device__ __forceinline__ float act(float a, float b) {
+__device__ __forceinline__ float act_exact(float a, float b) {
     if constexpr (MODE == SILU_MUL) {
         const float s = __fdiv_rn(a, __fadd_rn(1.0f, pinned_expf(-a)));
         return __fmul_rn(s, b);
@@ -26,6 +31,31 @@ __device__ __forceinline__ float act(float a, float b) {
     } else {  // a = y, b = z
         return __fdiv_rn(a, __fadd_rn(1.0f, pinned_expf(-b)));
     }
+}
+
+// fp16 / bf16 results: exp2 and reciprocal from the special-function unit.
+// The fp32 value is within a few 1e-6 (relative) of the exact one, far
+// below half an fp16 / bf16 unit in the last place, so the stored result
+// matches the exact one or is one unit away.  e^-x overflowing to +inf
+// gives x * 0 = -0 for large negative x, as x / inf does.
+__device__ __forceinline__ float sigmoid_den_fast(float x) {
+    return __fadd_rn(1.0f, exp2f_approx(__fmul_rn(x, -1.44269504088896340736f)));
+}
+template <int MODE>
+__device__ __forceinline__ float act_fast(float a, float b) {
+    if constexpr (MODE == SILU_MUL) {
+        return __fmul_rn(__fmul_rn(a, rcp_approx(sigmoid_den_fast(a))), b);
+    } else if constexpr (MODE == SILU) {
+        return __fmul_rn(a, rcp_approx(sigmoid_den_fast(a)));
+    } else {
+        return __fmul_rn(a, rcp_approx(sigmoid_den_fast(b)));
+    }
+}
+
+template <typename T, int MODE>
+__device__ __forceinline__ float act(float a, float b) {
+    if constexpr (sizeof(typename T::storage) == 4) return act_exact<MODE>(a, b);
+    else return act_fast<MODE>(a, b);
 }
 
 constexpr int kActThreads = 256;
@@ -76,7 +106,7 @@ act_vec_kernel(const ActArgs p) {
             unpack<T>(av[u], x);
             if constexpr (MODE != SILU) unpack<T>(bv[u], y);
 #pragma unroll
-            for (int e = 0; e < V; e++) x[e] = act<MODE>(x[e], MODE != SILU ? y[e] : 0.0f);
+            for (int e = 0; e < V; e++) x[e] = act<T, MODE>(x[e], MODE != SILU ? y[e] : 0.0f);
             st_stream((S*)p.out + r[u] * p.out_stride + c[u], pack<T>(x));
         }
     }
@@ -92,7 +122,7 @@ act_scalar_kernel(const ActArgs p) {
         const int64_t r = i / p.n, c = i - r * p.n;
         const float x = T::to_f(((const S*)p.a)[r * p.a_stride + c]);
         const float y = MODE != SILU ? T::to_f(((const S*)p.b)[r * p.b_stride + c]) : 0.0f;
-        ((S*)p.out)[r * p.out_stride + c] = T::from_f(act<MODE>(x, y));
+        ((S*)p.out)[r * p.out_stride + c] = T::from_f(act<T, MODE>(x, y));
     }
 }
 

@@ -75,7 +75,8 @@ def test_gather_vs_oracle(ane, oracle, tdt, hidden):
     if tdt != "f32":
         got32 = ane.embedding_gather(tt, torch.from_numpy(ids).cuda(), out_dtype=torch.float32)
         want32, _ = oracle.embedding_gather(table, ids, out_dtype=0)
-        assert np.array_equal(got32.cpu().numpy(), want32)
+        # compare bit patterns: random BF16 inputs include NaNs
+        assert np.array_equal(got32.cpu().numpy().view(np.uint32), want32.view(np.uint32))
 
 
 def test_gather_bad_ids_zero_row_and_flag(ane):

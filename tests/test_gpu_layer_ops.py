@@ -154,8 +154,14 @@ def test_silu_mul(ane, oracle, dt, shape):
     u = rand(rng, shape, dt)
     out = ane.silu_mul(to_dev(g, dt), to_dev(u, dt))
     want = oracle.silu_mul(g, u)
-    frac = check(to_host(out, dt), want, dt, "silu")
-    assert frac == 1.0  # pinned exp + IEEE divide: bit-exact
+    got = to_host(out, dt)
+    check(got, want, dt, "silu")
+    if dt == "f32":
+        # pinned exp + IEEE divide: bit-exact with the oracle
+        assert np.array_equal(got.view(np.int32), want.view(np.int32))
+    else:
+        # exp2 / reciprocal from the special-function unit: one unit at most
+        assert ulp(got, want, dt).max() <= 1
 
 
 def test_silu_extremes(ane, oracle):
