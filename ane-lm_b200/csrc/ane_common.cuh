@@ -101,16 +101,23 @@ __device__ __forceinline__ float pinned_expf(float x) {
     return __fmul_rn(p, pow2i(ki));
 }
 
-// 2^x and 1/x from the special-function unit (ex2.approx.ftz, rcp.approx.ftz):
-// a few ulp of fp32, used only where the result is rounded to 16 bits.
+// 2^x and 1/x from the special-function unit (ex2.approx, rcp.approx): a few
+// ulp of fp32, used only where the result is rounded to 16 bits.  FTZ picks
+// the flush-to-zero forms, cheaper, and exact enough when the stored type
+// cannot represent fp32 subnormals anyway (fp16); bf16 keeps fp32's
+// exponent range and needs the subnormal-preserving forms.
+template <bool FTZ>
 __device__ __forceinline__ float exp2f_approx(float x) {
     float y;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    if constexpr (FTZ) asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    else asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
+template <bool FTZ>
 __device__ __forceinline__ float rcp_approx(float x) {
     float y;
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    if constexpr (FTZ) asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    else asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
 

@@ -29,4 +29,8 @@ inline bool valid_dtype(int dtype) {
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
+// Grid size for a grid-stride kernel: `want` blocks, capped at what is
+// resident at once (SMs x blocks per SM), so the grid is a single wave.
+int resident_grid(const void* kernel, int threads, size_t smem, int64_t want);
+
 }  // namespace ane

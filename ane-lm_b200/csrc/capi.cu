@@ -37,6 +37,16 @@ int sm_count() {
     return cache[dev];
 }
 
+int resident_grid(const void* kernel, int threads, size_t smem, int64_t want) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+        per_sm <= 0)
+        per_sm = 1;
+    const int64_t cap = (int64_t)per_sm * sm_count();
+    if (want < 1) want = 1;
+    return (int)(want < cap ? want : cap);
+}
+
 }  // namespace ane
 
 extern "C" {

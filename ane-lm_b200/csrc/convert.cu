@@ -3,13 +3,13 @@
 //
 // HBM-bound streaming kernel: 2 bytes read + 2 bytes written per element.
 // Each thread moves 16-byte vectors (8 elements) with evict-first loads and
-// stores, UNROLL vectors in flight, over a grid sized to the SM count.
+// stores, kConvUnroll vectors in flight, over a grid of one resident wave.
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
 namespace ane {
 
-// One element: exponent re-bias by -112; e >= 31 (Inf/NaN included) ->
+// One element (scalar tail): exponent re-bias by -112; e >= 31 (Inf/NaN included) ->
 // signed Inf; 1 <= e <= 30 -> e<<10 | top 7 mantissa bits << 3;
 // -10 <= e <= 0 -> (1.m << 16) >> (14 - e), i.e. the hidden-bit mantissa
 // shifted right by (1 - e) and then by 13, truncating; below -> signed 0.
@@ -29,8 +29,18 @@ __device__ __forceinline__ uint32_t bf16_to_f16_bits(uint32_t b) {
     return sign | r;
 }
 
+// Two elements at once.  Round-toward-zero conversion of the exact fp32
+// value is the reference's truncation, subnormals included (it drops the
+// bits below 2^-24, and below 2^-25 nothing is left); it differs only where
+// the reference saturates: |x| >= 65536, Inf and NaN become signed Inf
+// (round-toward-zero would give 65504 or NaN), fixed up with a mask.
 __device__ __forceinline__ uint32_t cvt_pair(uint32_t w) {
-    return bf16_to_f16_bits(w & 0xFFFFu) | (bf16_to_f16_bits(w >> 16) << 16);
+    const float lo = __uint_as_float(w << 16);
+    const float hi = __uint_as_float(w & 0xFFFF0000u);
+    uint32_t r;
+    asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    const uint32_t big = __vcmpgeu2(w & 0x7FFF7FFFu, 0x47804780u);  // 0xFFFF per saturating half
+    return (r & ~big) | (((w & 0x80008000u) | 0x7C007C00u) & big);
 }
 
 __device__ __forceinline__ uint4 cvt_vec(uint4 v) {
@@ -77,7 +87,7 @@ extern "C" int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t n
     if (is_aligned(out, 16) && is_aligned(in, 16) && n >= 8) {
         const int64_t nvec = n / 8;
         const int64_t want = (nvec + kConvThreads * kConvUnroll - 1) / (kConvThreads * kConvUnroll);
-        const int blocks = (int)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+        const int blocks = resident_grid((const void*)bf16_to_f16_vec_kernel, kConvThreads, 0, want);
         bf16_to_f16_vec_kernel<<<blocks, kConvThreads, 0, s>>>(
             reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(in), nvec);
         done = nvec * 8;

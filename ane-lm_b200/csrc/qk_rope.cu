@@ -2,19 +2,17 @@
 // (models/llm/qwen3.cpp:444-473; core/cpu_ops.cpp:43-80).
 //
 // Fast path (rot_dim == head_dim, head_dim / kVec a power of two in
-// [2, 32], 16-byte aligned rows): one warp per unit of about 8 heads of a
-// row.  A head is served by
+// [2, 32], 16-byte aligned rows): one warp per row.  A head is served by
 // GL = chunks/2 lanes; lane l of the group holds chunk l (elements
 // [l*V, l*V+V), first half) and chunk l + GL (the RoPE partners j + half).
 // With that layout
 //   - the first butterfly stage of the pinned sum-of-squares order
 //     (offset GL) is an add inside the lane, the rest are xor shuffles
 //     inside the group; no shuffle is needed for RoPE;
-//   - the lane's cos/sin for j in [l*V, l*V+V) serve every head of the unit,
-//     so they are computed once per unit, in registers;
-//   - the lane's norm weights are the same for every q (k) head: loaded
-//     once per unit as 16-byte vectors.
-// All of the unit's heads are loaded before any math.
+//   - the lane's cos/sin for j in [l*V, l*V+V) serve every head of the row,
+//     so they are computed once per row, in registers;
+//   - the lane's norm weights are the same for every q (k) head: staged
+//     once per CTA in shared memory.
 //
 // Generic path (partial RoPE, other head sizes, unaligned rows, or the
 // caller-supplied cos/sin rows of apply_rope_cached): one warp per
@@ -47,123 +45,131 @@ struct QkArgs {
     const float* sin_row;
 };
 
-// A work unit is IPU head iterations (IPU * hpw heads) of one row; one
-// warp per unit, 8 warps per CTA.  Small units keep the register footprint
-// low (many warps per SM hide the load latency) while every unit still
-// moves 2 KB or more with 16-byte accesses.
-constexpr int kUnitWarps = 8;
+// One warp per row.  The row's heads stream through a ring of D register
+// slots: iteration `it` (HPW heads) is consumed from slot it % D, which is
+// refilled with iteration it + D straight away, so D iterations of loads
+// stay in flight while the warp computes.  Per-row setup (position,
+// cos/sin) is paid once for all heads of the row.  GL (lanes per head) is a
+// template parameter so that every index is a constant; the frequency table
+// and the norm weights are staged once per CTA in shared memory.
+constexpr int kRowWarps = 4;
 
-template <typename T, int IPU>
-__global__ void __launch_bounds__(kUnitWarps * kWarp)
-qk_norm_rope_unit_kernel(const QkArgs a, const RopeFreq fr, const int gl_log2,
-                         const int units_per_row, const bool pow2_dim) {
+template <typename T, int GL, int D>
+__global__ void __launch_bounds__(kRowWarps * kWarp, 8)
+qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim) {
     using S = typename T::storage;
     constexpr int V = T::kVec;
+    constexpr int HPW = kWarp / GL;                  // heads per iteration
+    constexpr int HALF = GL * V;                     // rot_dim / 2 = head_dim / 2
+    constexpr int CPL = HALF >= 32 ? HALF / 32 : V;  // cos/sin computed per lane
+    __shared__ __align__(16) float s_freq[HALF];
+    __shared__ __align__(16) float s_w[2][2 * HALF];
+    for (int i = threadIdx.x; i < HALF; i += blockDim.x) s_freq[i] = fr.f[i];
+    if (a.qw != nullptr) {
+        for (int i = threadIdx.x; i < 2 * HALF; i += blockDim.x) {
+            s_w[0][i] = __ldg(a.qw + i);
+            s_w[1][i] = __ldg(a.kw + i);
+        }
+    }
+    __syncthreads();
     const int lane = threadIdx.x & 31;
-    const int64_t unit = (int64_t)blockIdx.x * kUnitWarps + (threadIdx.x >> 5);
-    if (unit >= a.rows * units_per_row) return;
-    const int64_t row = unit / units_per_row;
-    const int GL = 1 << gl_log2;           // lanes per head
-    const int hpw = kWarp >> gl_log2;      // heads per iteration
-    const int g = lane >> gl_log2;         // head slot of this lane
-    const int l = lane & (GL - 1);         // lane within the head group
-    const int half = GL * V;               // rot_dim / 2
-    const int nh = a.n_q + a.n_kv;
-    const int head0 = (int)(unit - row * units_per_row) * IPU * hpw;
-    S* qrow = (S*)a.q + row * a.q_row_stride;
-    S* krow = (S*)a.k + row * a.k_row_stride;
+    const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    if (row >= a.rows) return;
+    const int g = lane / GL;  // head slot of this lane
+    const int l = lane % GL;  // lane within the head group
+    const int nq = a.n_q, nh = a.n_q + a.n_kv;
+    const int nit = (nh + HPW - 1) / HPW;
+    S* const qrow = (S*)a.q + row * a.q_row_stride;
+    S* const krow = (S*)a.k + row * a.k_row_stride;
+    const int qhs = a.q_head_stride, khs = a.k_head_stride;
+    auto head_ptr = [&](int h) -> S* { return h < nq ? qrow + h * qhs : krow + (h - nq) * khs; };
 
-    uint4 lo[IPU], hi[IPU];
+    uint4 lo[D], hi[D];
 #pragma unroll
-    for (int it = 0; it < IPU; it++) {
-        const int h = head0 + it * hpw + g;
+    for (int d = 0; d < D; d++) {
+        const int h = d * HPW + g;
         if (h < nh) {
-            const S* base = h < a.n_q ? qrow + (int64_t)h * a.q_head_stride
-                                      : krow + (int64_t)(h - a.n_q) * a.k_head_stride;
-            lo[it] = ld_stream(base + l * V);
-            hi[it] = ld_stream(base + half + l * V);
+            const S* p = head_ptr(h);
+            lo[d] = ld_stream(p + l * V);
+            hi[d] = ld_stream(p + HALF + l * V);
         }
     }
 
-    // cos/sin of the lane's V frequencies at the row's position.  The hpw
-    // lanes sharing l need the same values: each computes cpl of them and
+    // cos/sin of the lane's V frequencies at the row's position.  The HPW
+    // lanes sharing l need the same values: each computes CPL of them and
     // the rest arrive by shuffle.
     const float fpos = (float)(a.positions ? __ldg(a.positions + row) : a.pos);
-    const int cpl = half >= 32 ? half / 32 : V;
     float cs[V], sn[V];
-    if (cpl == V) {
+    if constexpr (CPL == V) {
 #pragma unroll
-        for (int e = 0; e < V; e++) pinned_sincosf(__fmul_rn(fpos, fr.f[l * V + e]), &sn[e], &cs[e]);
+        for (int e = 0; e < V; e++) pinned_sincosf(__fmul_rn(fpos, s_freq[l * V + e]), &sn[e], &cs[e]);
     } else {
-        float mc[4], ms[4];
+        float mc[CPL], ms[CPL];
 #pragma unroll
-        for (int c = 0; c < 4; c++)
-            if (c < cpl) pinned_sincosf(__fmul_rn(fpos, fr.f[l * V + g * cpl + c]), &ms[c], &mc[c]);
+        for (int c = 0; c < CPL; c++)
+            pinned_sincosf(__fmul_rn(fpos, s_freq[l * V + g * CPL + c]), &ms[c], &mc[c]);
 #pragma unroll
         for (int e = 0; e < V; e++) {
-            const int src = (e / cpl) * GL + l;
-            float vc = mc[0], vs = ms[0];
-#pragma unroll
-            for (int c = 1; c < 4; c++)
-                if (e % cpl == c) { vc = mc[c]; vs = ms[c]; }
-            cs[e] = __shfl_sync(0xffffffffu, vc, src);
-            sn[e] = __shfl_sync(0xffffffffu, vs, src);
+            cs[e] = __shfl_sync(0xffffffffu, mc[e % CPL], (e / CPL) * GL + l);
+            sn[e] = __shfl_sync(0xffffffffu, ms[e % CPL], (e / CPL) * GL + l);
         }
     }
 
     const bool norm = a.qw != nullptr;
-    float w0[V], w1[V];
-    int wtype = -1;  // 0: q weights loaded, 1: k weights loaded
-    const float inv_dim = 1.0f / (float)a.head_dim;
+    const float inv_dim = 1.0f / (float)(2 * HALF);
+    for (int it0 = 0; it0 < nit; it0 += D) {
 #pragma unroll
-    for (int it = 0; it < IPU; it++) {
-        const int h = head0 + it * hpw + g;
-        if (head0 + it * hpw >= nh) break;  // warp-uniform
-        const bool live = h < nh;
-        float x0[V], x1[V];
-        if (live) {
-            unpack<T>(lo[it], x0);
-            unpack<T>(hi[it], x1);
-        } else {
+        for (int d = 0; d < D; d++) {
+            if (it0 + d >= nit) break;  // warp-uniform
+            const int h = (it0 + d) * HPW + g;
+            const bool live = h < nh;
+            float x0[V], x1[V];
+            if (live) {
+                unpack<T>(lo[d], x0);
+                unpack<T>(hi[d], x1);
+            } else {
 #pragma unroll
-            for (int e = 0; e < V; e++) { x0[e] = 0.0f; x1[e] = 0.0f; }
-        }
-        if (norm) {
-            float acc = __fadd_rn(sumsq_chain<V>(x0, 0.0f), sumsq_chain<V>(x1, 0.0f));
-            for (int off = GL >> 1; off >= 1; off >>= 1)
-                acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-            // ss / dim is exact as a multiply when dim is a power of two
-            const float mean = pow2_dim ? __fmul_rn(acc, inv_dim) : __fdiv_rn(acc, (float)a.head_dim);
-            const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-            const int want = h < a.n_q ? 0 : 1;
-            if (want != wtype) {
-                const float* wsrc = want == 0 ? a.qw : a.kw;
+                for (int e = 0; e < V; e++) { x0[e] = 0.0f; x1[e] = 0.0f; }
+            }
+            const int hn = h + D * HPW;  // refill the slot D iterations ahead
+            if (hn < nh) {
+                const S* q = head_ptr(hn);
+                lo[d] = ld_stream(q + l * V);
+                hi[d] = ld_stream(q + HALF + l * V);
+            }
+            if (norm) {
+                float acc = __fadd_rn(sumsq_chain<V>(x0, 0.0f), sumsq_chain<V>(x1, 0.0f));
+#pragma unroll
+                for (int off = GL / 2; off >= 1; off >>= 1)
+                    acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+                // ss / dim is exact as a multiply when dim is a power of two
+                const float mean = pow2_dim ? __fmul_rn(acc, inv_dim) : __fdiv_rn(acc, (float)(2 * HALF));
+                const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+                const float* w = s_w[h < nq ? 0 : 1];
 #pragma unroll
                 for (int q4 = 0; q4 < V / 4; q4++) {
-                    const float4 t0 = __ldg(reinterpret_cast<const float4*>(wsrc + l * V) + q4);
-                    const float4 t1 = __ldg(reinterpret_cast<const float4*>(wsrc + half + l * V) + q4);
-                    w0[4 * q4] = t0.x; w0[4 * q4 + 1] = t0.y; w0[4 * q4 + 2] = t0.z; w0[4 * q4 + 3] = t0.w;
-                    w1[4 * q4] = t1.x; w1[4 * q4 + 1] = t1.y; w1[4 * q4 + 2] = t1.z; w1[4 * q4 + 3] = t1.w;
+                    const float4 t0 = reinterpret_cast<const float4*>(w + l * V)[q4];
+                    const float4 t1 = reinterpret_cast<const float4*>(w + HALF + l * V)[q4];
+                    const float w0[4] = {t0.x, t0.y, t0.z, t0.w};
+                    const float w1[4] = {t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        x0[4 * q4 + e] = __fmul_rn(__fmul_rn(x0[4 * q4 + e], inv), w0[e]);
+                        x1[4 * q4 + e] = __fmul_rn(__fmul_rn(x1[4 * q4 + e], inv), w1[e]);
+                    }
                 }
-                wtype = want;
             }
+            if (live) {
+                float y0[V], y1[V];
 #pragma unroll
-            for (int e = 0; e < V; e++) {
-                x0[e] = __fmul_rn(__fmul_rn(x0[e], inv), w0[e]);
-                x1[e] = __fmul_rn(__fmul_rn(x1[e], inv), w1[e]);
+                for (int e = 0; e < V; e++) {
+                    y0[e] = __fsub_rn(__fmul_rn(x0[e], cs[e]), __fmul_rn(x1[e], sn[e]));
+                    y1[e] = __fadd_rn(__fmul_rn(x1[e], cs[e]), __fmul_rn(x0[e], sn[e]));
+                }
+                S* q = head_ptr(h);
+                st_stream(q + l * V, pack<T>(y0));
+                st_stream(q + HALF + l * V, pack<T>(y1));
             }
-        }
-        if (live) {
-            float y0[V], y1[V];
-#pragma unroll
-            for (int e = 0; e < V; e++) {
-                y0[e] = __fsub_rn(__fmul_rn(x0[e], cs[e]), __fmul_rn(x1[e], sn[e]));
-                y1[e] = __fadd_rn(__fmul_rn(x1[e], cs[e]), __fmul_rn(x0[e], sn[e]));
-            }
-            S* base = h < a.n_q ? qrow + (int64_t)h * a.q_head_stride
-                                : krow + (int64_t)(h - a.n_q) * a.k_head_stride;
-            st_stream(base + l * V, pack<T>(y0));
-            st_stream(base + half + l * V, pack<T>(y1));
         }
     }
 }
@@ -173,7 +179,7 @@ constexpr int kGenericMaxHead = 1024;
 
 template <typename T>
 __global__ void __launch_bounds__(kQkWarps * kWarp)
-qk_norm_rope_generic_kernel(const QkArgs a, const RopeFreq fr) {
+qk_norm_rope_generic_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr) {
     using S = typename T::storage;
     constexpr int V = T::kVec;
     __shared__ float sm[kQkWarps][kGenericMaxHead];
@@ -250,20 +256,18 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s) {
                 gl_log2 >= 0 && nchunk <= 32 && is_aligned(a.q, 16) && is_aligned(a.k, 16) &&
                 (a.q_row_stride * es) % 16 == 0 && (a.k_row_stride * es) % 16 == 0 &&
                 (a.q_head_stride * es) % 16 == 0 && (a.k_head_stride * es) % 16 == 0;
-    if (fast && (!a.qw || (is_aligned(a.qw, 16) && is_aligned(a.kw, 16)))) {
-        const int hpw = kWarp >> gl_log2;
-        const int ipu = hpw >= 8 ? 1 : 8 / hpw;   // about 8 heads per unit
-        const int units_per_row = (nh + ipu * hpw - 1) / (ipu * hpw);
-        const int64_t units = a.rows * units_per_row;
-        const unsigned blocks = (unsigned)((units + kUnitWarps - 1) / kUnitWarps);
+    if (fast) {
+        const unsigned blocks = (unsigned)((a.rows + kRowWarps - 1) / kRowWarps);
         const bool pow2 = (a.head_dim & (a.head_dim - 1)) == 0;
-#define ANE_QK_UNIT(N) \
-    qk_norm_rope_unit_kernel<T, N><<<blocks, kUnitWarps * kWarp, 0, s>>>(a, fr, gl_log2, units_per_row, pow2)
-        if (ipu == 1) ANE_QK_UNIT(1);
-        else if (ipu == 2) ANE_QK_UNIT(2);
-        else if (ipu == 4) ANE_QK_UNIT(4);
-        else ANE_QK_UNIT(8);
-#undef ANE_QK_UNIT
+#define ANE_QK_ROW(GLV) qk_norm_rope_row_kernel<T, GLV, 2><<<blocks, kRowWarps * kWarp, 0, s>>>(a, fr, pow2)
+        switch (gl_log2) {
+            case 0: ANE_QK_ROW(1); break;
+            case 1: ANE_QK_ROW(2); break;
+            case 2: ANE_QK_ROW(4); break;
+            case 3: ANE_QK_ROW(8); break;
+            default: ANE_QK_ROW(16); break;
+        }
+#undef ANE_QK_ROW
     } else {
         if (a.head_dim > kGenericMaxHead)
             return fail(ANE_CUDA_ERR_UNSUPPORTED, "qk_norm_rope: head_dim %d > %d", a.head_dim,

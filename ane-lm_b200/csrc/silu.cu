@@ -15,6 +15,8 @@
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
+#include <type_traits>
+
 namespace ane {
 
 enum ActMode { SILU_MUL = 0, SILU = 1, MUL_SIGMOID = 2 };
@@ -37,28 +39,31 @@ __device__ __forceinline__ float act_exact(float a, float b) {
 // The fp32 value is within a few 1e-6 (relative) of the exact one, far
 // below half an fp16 / bf16 unit in the last place, so the stored result
 // matches the exact one or is one unit away.  e^-x overflowing to +inf
-// gives x * 0 = -0 for large negative x, as x / inf does.
+// gives x * 0 = -0 for large negative x, as x / inf does.  fp16 (FTZ)
+// cannot hold the fp32 subnormals that the flushing forms drop; bf16 can.
+template <bool FTZ>
 __device__ __forceinline__ float sigmoid_den_fast(float x) {
-    return __fadd_rn(1.0f, exp2f_approx(__fmul_rn(x, -1.44269504088896340736f)));
+    return __fadd_rn(1.0f, exp2f_approx<FTZ>(__fmul_rn(x, -1.44269504088896340736f)));
 }
-template <int MODE>
+template <int MODE, bool FTZ>
 __device__ __forceinline__ float act_fast(float a, float b) {
     if constexpr (MODE == SILU_MUL) {
-        return __fmul_rn(__fmul_rn(a, rcp_approx(sigmoid_den_fast(a))), b);
+        return __fmul_rn(__fmul_rn(a, rcp_approx<FTZ>(sigmoid_den_fast<FTZ>(a))), b);
     } else if constexpr (MODE == SILU) {
-        return __fmul_rn(a, rcp_approx(sigmoid_den_fast(a)));
+        return __fmul_rn(a, rcp_approx<FTZ>(sigmoid_den_fast<FTZ>(a)));
     } else {
-        return __fmul_rn(a, rcp_approx(sigmoid_den_fast(b)));
+        return __fmul_rn(a, rcp_approx<FTZ>(sigmoid_den_fast<FTZ>(b)));
     }
 }
 
 template <typename T, int MODE>
 __device__ __forceinline__ float act(float a, float b) {
     if constexpr (sizeof(typename T::storage) == 4) return act_exact<MODE>(a, b);
-    else return act_fast<MODE>(a, b);
+    else return act_fast<MODE, std::is_same<T, F16>::value>(a, b);
 }
 
 constexpr int kActThreads = 256;
+constexpr int kActUnroll = 2;  // 16-byte vectors per thread in flight, per input
 
 struct ActArgs {
     void* out;
@@ -79,12 +84,13 @@ act_vec_kernel(const ActArgs p) {
     const int64_t nvec = p.n / V;
     const int64_t total = p.rows * nvec;
     const int64_t stride = (int64_t)gridDim.x * kActThreads;
-    for (int64_t i = (int64_t)blockIdx.x * kActThreads + threadIdx.x; i < total; i += 2 * stride) {
-        uint4 av[2], bv[2];
-        int64_t r[2], c[2];
-        bool ok[2];
+    for (int64_t i = (int64_t)blockIdx.x * kActThreads + threadIdx.x; i < total;
+         i += kActUnroll * stride) {
+        uint4 av[kActUnroll], bv[kActUnroll];
+        int64_t r[kActUnroll], c[kActUnroll];
+        bool ok[kActUnroll];
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
+        for (int u = 0; u < kActUnroll; u++) {
             const int64_t j = i + u * stride;
             ok[u] = j < total;
             if constexpr (FLAT) {
@@ -100,7 +106,7 @@ act_vec_kernel(const ActArgs p) {
             }
         }
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
+        for (int u = 0; u < kActUnroll; u++) {
             if (!ok[u]) continue;
             float x[V], y[V];
             unpack<T>(av[u], x);
@@ -140,9 +146,11 @@ static int launch_act(ActArgs p, cudaStream_t s) {
         p.rows = 1;
     }
     const int64_t items = vec ? p.rows * (p.n / V) : p.rows * p.n;
-    const int64_t want = (items + 2 * kActThreads - 1) / (2 * kActThreads);
-    const int64_t cap = (int64_t)sm_count() * 8;
-    const int blocks = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+    const int64_t want = (items + kActUnroll * kActThreads - 1) / (kActUnroll * kActThreads);
+    const void* k = vec ? (p.rows == 1 ? (const void*)act_vec_kernel<T, MODE, true>
+                                       : (const void*)act_vec_kernel<T, MODE, false>)
+                        : (const void*)act_scalar_kernel<T, MODE>;
+    const int blocks = resident_grid(k, kActThreads, 0, want);
     if (vec && p.rows == 1) act_vec_kernel<T, MODE, true><<<blocks, kActThreads, 0, s>>>(p);
     else if (vec) act_vec_kernel<T, MODE, false><<<blocks, kActThreads, 0, s>>>(p);
     else act_scalar_kernel<T, MODE><<<blocks, kActThreads, 0, s>>>(p);

@@ -171,3 +171,25 @@ def test_silu_extremes(ane, oracle):
     out = ane.silu_mul(to_dev(g, "f32"), to_dev(u, "f32"))
     want = oracle.silu_mul(g, u)
     assert np.array_equal(to_host(out, "f32").view(np.int32), want.view(np.int32))
+
+
+def test_silu_tiny_results_bf16(ane, oracle):
+    # bf16 keeps fp32's exponent range: gates near -88 give results near 1e-37
+    g = np.array([[-80.0, -85.0, -86.5, -87.0, -87.5, -88.0, -88.5, -89.0, -95.0, -120.0]],
+                 np.float32)
+    gb = (g.view(np.uint32) >> 16).astype(np.uint16)
+    ub = (np.ones_like(g).view(np.uint32) >> 16).astype(np.uint16)
+    out = to_host(ane.silu_mul(to_dev(gb, "bf16"), to_dev(ub, "bf16")), "bf16")
+    want = oracle.silu_mul(gb, ub)
+    assert ulp(out, want, "bf16").max() <= 1, (out, want)
+
+
+def test_silu_extremes_f16(ane, oracle):
+    g = np.array([[0.0, -0.0, -100.0, 100.0, -88.0, 88.0, -250.0, 250.0, 1e-7, -1e-7,
+                   60000.0, -60000.0, 3.0, -3.0, 0.5, -0.5, -17.0, -12.0, 6e-5, -6e-5]],
+                 np.float16)
+    u = np.array([[1.0, -1.0] * 10], np.float16)
+    out = to_host(ane.silu_mul(to_dev(g, "f16"), to_dev(u, "f16")), "f16")
+    want = oracle.silu_mul(g, u)
+    assert f16_ulp_diff(out, want).max() <= 1
+    assert np.array_equal(np.signbit(out), np.signbit(want))
