@@ -600,6 +600,45 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_ncu_case(cases, rows=16384):
+    """Small cases for ncu captures: each kernel launched twice (a warm launch
+    and the one to capture); inputs above L2, a few GB on the device."""
+    import ctypes as C
+    torch, ane, _, _ = _setup_gpu(1)
+    L = ane.lib()
+    cur = torch.cuda.current_stream()
+    sp = C.c_void_p(cur.cuda_stream)
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    if "chain" in cases:
+        b = make_chain_inputs(torch, rows, HIDDEN, NQ, NKV, HD, INTER, SEQ, 1)
+        ch = Chain(ane, b, rows, HIDDEN, NQ, NKV, HD, INTER, cur.cuda_stream)
+        for _ in range(2):
+            ch.launch()
+            torch.cuda.synchronize()
+        del b, ch
+    if "convert" in cases:
+        n = 1 << 29
+        src = torch.randint(-32768, 32768, (n,), dtype=torch.int16, device="cuda")
+        dst = torch.empty_like(src)
+        for _ in range(2):
+            assert L.ane_cuda_bf16_to_f16(P(dst), P(src), n, sp) == 0
+        torch.cuda.synchronize()
+        del src, dst
+    if "sampler" in cases:
+        r, v = 256, 151936
+        g = torch.Generator(device="cuda").manual_seed(3)
+        logits = torch.randn(r, v, device="cuda", generator=g) * 3
+        hist = torch.randint(0, v, (r, 1024), device="cuda", dtype=torch.int32, generator=g)
+        hlen = torch.full((r,), 1024, device="cuda", dtype=torch.int32)
+        u = torch.rand(r, device="cuda", generator=g)
+        tok = torch.empty(r, device="cuda", dtype=torch.int32)
+        for _ in range(2):
+            assert L.ane_cuda_sample_rows(P(logits), r, v, v, P(hist), P(hlen), 1024, P(u), 0.6,
+                                          1.2, 256, 0.1, P(tok), sp) == 0
+        torch.cuda.synchronize()
+    print("ncu case done:", ",".join(sorted(cases)), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -608,7 +647,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--ncu-case", default="",
+                    help="comma list of chain,convert,sampler: run the small profiling case and exit")
     args = ap.parse_args()
+    if args.ncu_case:
+        run_ncu_case(set(args.ncu_case.split(",")))
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
