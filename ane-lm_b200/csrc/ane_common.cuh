@@ -121,6 +121,29 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return y;
 }
 
+// pinned_expf for x <= 0 (softmax arguments x - max), without branches:
+// the same operations in the same order as pinned_expf, so the same bits for
+// every x in [-inf, 0]; the two-step subnormal scaling is selected, not
+// branched.  NaN arguments are outside its contract.
+__device__ __forceinline__ float pinned_expf_nonpos(float x) {
+    const float xc = fmaxf(x, -104.0f);
+    const float k = rintf(__fmul_rn(xc, 1.44269502162933349609375f));
+    float r = __fmaf_rn(-k, 0.693147182464599609375f, xc);
+    r = __fmaf_rn(-k, -1.904654212125933608e-09f, r);
+    float p = __fmaf_rn(0.00019841270113829523324966431f, r, 0.0013888889225199818611145020f);
+    p = __fmaf_rn(p, r, 0.0083333337679505348205566406f);
+    p = __fmaf_rn(p, r, 0.041666667908430099487304688f);
+    p = __fmaf_rn(p, r, 0.16666667163372039794921875f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int ki = (int)k;
+    const bool sub = ki < -126;
+    float y = __fmul_rn(p, pow2i(sub ? ki + 64 : ki));
+    y = sub ? __fmul_rn(y, pow2i(-64)) : y;
+    return x < -104.0f ? 0.0f : y;
+}
+
 // ---------------------------------------------------------------------
 // sin / cos for RoPE: reduction by pi/2 in double (pi/2 as double head +
 // tail, two fma), reduced argument rounded to float, Taylor polynomials of

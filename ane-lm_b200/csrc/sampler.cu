@@ -1,15 +1,18 @@
 // sampler.cu -- batched sample_token (core/sampling.cpp:10-66) and softmax
-// (core/cpu_ops.cpp:83-99), one 1024-thread CTA per row.
+// (core/cpu_ops.cpp:83-99), one 512-thread CTA per row, two CTAs per SM so
+// that a batch of up to 2 x SMs rows runs in a single wave.
 //
 // Pass 0  the row's repetition window goes into a shared-memory hash
 //         (id -> count) and a vocabulary bitmap; each distinct id's logit is
 //         penalised once (rep, then freq), as sampling.cpp:17-42 does.
 // Pass 1  max of the penalised logits (argmax for temperature <= 0).
 //         max(fl(a * inv_t)) = fl(max(a) * inv_t) since rounding is monotone.
-// Pass 2  e = exp(fl(fl(a * inv_t) - max)) summed in the pinned order: group
-//         g of 4 consecutive elements belongs to thread g % 1024, which adds
-//         its elements in increasing order; an xor butterfly inside each warp,
-//         then over the 32 warp sums.
+// Pass 2  e = exp(d), d = fl(fl(a * inv_t) - max), summed in the pinned order
+//         of 1024 "virtual threads": group g of 4 consecutive elements belongs
+//         to virtual thread g % 1024, which adds its elements in increasing
+//         order; an xor butterfly inside each virtual warp of 32, then over
+//         the 32 virtual-warp sums.  Thread t of the CTA plays virtual threads
+//         t and t + 512, so the bits do not depend on the CTA size.
 // Pass 3  the inverse-CDF scan `cum += p[i]; if (cum >= r) return i`, with
 //         p = fl(e * (1/sum)), reproduced bit for bit in parallel.  While cum
 //         stays inside one binade [2^E, 2^(E+1)) (or below 2^-125), every fp32
@@ -21,15 +24,24 @@
 //         a real fp32 add, the binade is re-derived, and the tile resumes
 //         after it.  The first element whose running sum reaches r (in
 //         units: ceil(r / U)) is the token.
+//         Elements with d < T(E) = ln(U / (2 inv)) - 1e-4 have p < U / 2:
+//         they add 0 units, are no tie and cannot leave the binade, so their
+//         exp is never evaluated.  U only grows along the row, so an element
+//         found insignificant stays so.  The exps that are needed are
+//         compacted per warp through shared memory, so a warp evaluates
+//         ceil(significant / 32) exps per slot instead of one per element.
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
 namespace ane {
 
-constexpr int kSampThreads = 1024;
-constexpr int kSampWarps = kSampThreads / kWarp;
+constexpr int kSampThreads = 512;
+constexpr int kSampWarps = kSampThreads / kWarp;   // 16
+constexpr int kVirtThreads = 1024;                 // pinned softmax-sum order
+constexpr int kPerThread = 8;                      // CDF elements per thread per tile
+constexpr int kTile = kSampThreads * kPerThread;   // 4096
 constexpr int kMaxWindow = 4096;
-constexpr uint32_t kSat = 1u << 30;       // saturation of unit counts
+constexpr uint32_t kSat = 1u << 30;                // saturation of unit counts
 constexpr uint32_t kBinadeUnits = 1u << 24;
 constexpr uint32_t kNoEvent = 0xFFFFFFFFu;
 
@@ -56,15 +68,15 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) {
 
 // Shared state of one row.
 struct RowSmem {
-    float red_f[kSampWarps];
+    float red_f[kVirtThreads / kWarp];
     uint32_t red_u[kSampWarps];
     uint32_t wscan[kSampWarps];
     float bcast_f;
-    int bcast_i;
     // CDF state
     uint32_t ucum;   // running sum in units of U
     int E;           // binade exponent; U = 2^(E-23)
     uint32_t tr;     // ceil(r / U), saturated
+    float td;        // significance threshold on d for this binade
     int start;       // first element still to scan
     uint32_t ev;     // event code of this round
     int result;
@@ -86,27 +98,28 @@ __device__ __forceinline__ uint32_t slot_of(int32_t tok, int shift) {
 __device__ __forceinline__ float penalised(const Penalty& P, int i, float x) {
     if (P.bitmap[i >> 5] & (1u << (i & 31))) {
         uint32_t h = slot_of(i, P.shift);
-        while (P.keys[h] != i) h = (h + 1) & P.mask;
+        while (P.keys[h] != i) h = (h + 1) & P.mask;  // present: the bit is set
         return P.vals[h];
     }
     return x;
 }
 
-// Loads element group g (4 consecutive elements) with penalties applied;
-// elements past the vocabulary read as -inf and are never counted.
-__device__ __forceinline__ void load_group(const SampArgs& a, const float* row, const Penalty& P,
-                                           int g, float v[4]) {
-    const int base = g * 4;
-    if (a.vec) {
+// Elements base .. base+3 (base a multiple of 4) with penalties applied;
+// past the vocabulary: -inf.  The group's 4 bits share one bitmap word.
+__device__ __forceinline__ void load4(const SampArgs& a, const float* row, const Penalty& P,
+                                      int base, float v[4]) {
+    if (a.vec && base + 3 < a.vocab) {
         const float4 t = *reinterpret_cast<const float4*>(row + base);
         v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
     } else {
 #pragma unroll
         for (int e = 0; e < 4; e++) v[e] = base + e < a.vocab ? row[base + e] : -INFINITY;
     }
+    if (base < a.vocab && ((P.bitmap[base >> 5] >> (base & 31)) & 0xFu)) {
 #pragma unroll
-    for (int e = 0; e < 4; e++)
-        if (base + e < a.vocab) v[e] = penalised(P, base + e, v[e]);
+        for (int e = 0; e < 4; e++)
+            if (base + e < a.vocab) v[e] = penalised(P, base + e, v[e]);
+    }
 }
 
 // --- block reductions --------------------------------------------------------
@@ -116,7 +129,7 @@ __device__ __forceinline__ float block_max(float v, RowSmem& S) {
     if (lane == 0) S.red_f[w] = v;
     __syncthreads();
     if (w == 0) {
-        v = S.red_f[lane];
+        v = lane < kSampWarps ? S.red_f[lane] : -INFINITY;
         for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
         if (lane == 0) S.bcast_f = v;
     }
@@ -124,14 +137,21 @@ __device__ __forceinline__ float block_max(float v, RowSmem& S) {
     return S.bcast_f;
 }
 
-// The pinned order: xor butterfly in each warp, then over the warp sums.
-__device__ __forceinline__ float block_sum_pinned(float v, RowSmem& S) {
-    v = butterfly_sum(v, kWarp);
+// The pinned order over 1024 virtual threads: acc_lo belongs to virtual
+// thread t, acc_hi to t + 512.  Butterfly inside each virtual warp, then over
+// the 32 virtual-warp sums (virtual warp w is real warp w for acc_lo and real
+// warp w - 16 for acc_hi).
+__device__ __forceinline__ float block_sum_pinned(float acc_lo, float acc_hi, RowSmem& S) {
+    const float lo = butterfly_sum(acc_lo, kWarp);
+    const float hi = butterfly_sum(acc_hi, kWarp);
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) S.red_f[w] = v;
+    if (lane == 0) {
+        S.red_f[w] = lo;
+        S.red_f[w + kSampWarps] = hi;
+    }
     __syncthreads();
     if (w == 0) {
-        v = butterfly_sum(S.red_f[lane], kWarp);
+        const float v = butterfly_sum(S.red_f[lane], kWarp);
         if (lane == 0) S.bcast_f = v;
     }
     __syncthreads();
@@ -157,7 +177,7 @@ __device__ Penalty build_penalties(const SampArgs& a, int64_t row, const float* 
             const int32_t tok = __ldg(h + j);
             if (tok < 0 || tok >= a.vocab) continue;
             uint32_t s = slot_of(tok, P.shift);
-            while (true) {
+            while (true) {  // the table has at least twice the window's slots
                 const int32_t prev = atomicCAS(&keys[s], -1, tok);
                 if (prev == -1 || prev == tok) break;
                 s = (s + 1) & P.mask;
@@ -198,7 +218,7 @@ __device__ __forceinline__ void classify(float p, int E, uint32_t& k, bool& tie,
 }
 
 // Sets the binade state of S from an exact fp32 running sum `cum`.
-__device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r) {
+__device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, float inv) {
     const uint32_t b = __float_as_uint(cum);
     int e = (int)((b >> 23) & 0xFFu) - 127;
     if (e < -126) e = -126;
@@ -206,7 +226,7 @@ __device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r) {
     // cum / U: exact integer below 2^24
     const int pe = (int)((b >> 23) & 0xFFu);
     const uint32_t m = pe ? ((b & 0x7FFFFFu) | 0x800000u) : (b & 0x7FFFFFu);
-    const int s = (pe ? pe : 1) - 127 - e;  // 0 for normals; 0 for e = -126 subnormals
+    const int s = (pe ? pe : 1) - 127 - e;  // 0 for normals and for e = -126 subnormals
     S.ucum = m << s;
     // ceil(r / U)
     const uint32_t rb = __float_as_uint(r);
@@ -220,12 +240,20 @@ __device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r) {
     else if (-rs >= 25) tr = 1;
     else tr = (rm + (1u << -rs) - 1u) >> -rs;
     S.tr = tr < kSat ? tr : kSat;
+    // d < td  =>  exp(d) * inv < U / 2 with room for the exp's and the
+    // product's rounding (relative 2^-21) and for rounding td itself.  Below
+    // U / 2 = 2^-126 a product near U / 2 would be subnormal and its rounding
+    // no longer relative: no element is skipped there.
+    S.td = e - 24 >= -126 ? (float)(log(ldexp(1.0, e - 23) / (2.0 * (double)inv)) - 1e-4)
+                          : -INFINITY;
 }
 
-__global__ void __launch_bounds__(kSampThreads, 1)
+__global__ void __launch_bounds__(kSampThreads, 2)
 sample_rows_kernel(const SampArgs a) {
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ RowSmem S;
+    __shared__ float cbuf[kSampWarps][kWarp * kPerThread];       // compacted d, then p
+    __shared__ uint16_t cidx[kSampWarps][kWarp * kPerThread];    // their tile-local indices
     const int64_t row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int slots = 1 << a.slots_log2;
@@ -237,20 +265,20 @@ sample_rows_kernel(const SampArgs a) {
     const Penalty P = build_penalties(a, row, lrow, bitmap, keys, counts, vals);
     const int ngroups = (a.vocab + 3) >> 2;
 
-    // ---- pass 1: max / argmax ----
+    // ---- greedy: first maximum (core/sampling.cpp:45-52) ----
     if (a.temperature <= 0.0f) {
         float best = -INFINITY;
         int bi = 0x7FFFFFFF;
         for (int g = tid; g < ngroups; g += kSampThreads) {
             float v[4];
-            load_group(a, lrow, P, g, v);
+            load4(a, lrow, P, g * 4, v);
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int i = g * 4 + e;
                 if (i < a.vocab && (v[e] > best || bi == 0x7FFFFFFF)) { best = v[e]; bi = i; }
             }
         }
-        // first maximum: larger value wins, equal values -> smaller index
+        // larger value wins, equal values -> smaller index
         for (int off = 16; off >= 1; off >>= 1) {
             const float ob = __shfl_xor_sync(0xffffffffu, best, off);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
@@ -259,8 +287,8 @@ sample_rows_kernel(const SampArgs a) {
         if (lane == 0) { S.red_f[w] = best; S.red_u[w] = (uint32_t)bi; }
         __syncthreads();
         if (w == 0) {
-            best = S.red_f[lane];
-            bi = (int)S.red_u[lane];
+            best = lane < kSampWarps ? S.red_f[lane] : -INFINITY;
+            bi = lane < kSampWarps ? (int)S.red_u[lane] : 0x7FFFFFFF;
             for (int off = 16; off >= 1; off >>= 1) {
                 const float ob = __shfl_xor_sync(0xffffffffu, best, off);
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
@@ -270,131 +298,196 @@ sample_rows_kernel(const SampArgs a) {
         }
         return;
     }
+
+    // ---- pass 1: max, four groups in flight per thread ----
     float mx = -INFINITY;
-    for (int g = tid; g < ngroups; g += kSampThreads) {
-        float v[4];
-        load_group(a, lrow, P, g, v);
+    for (int g0 = 0; g0 < ngroups; g0 += 4 * kSampThreads) {
+        float v[4][4];
 #pragma unroll
-        for (int e = 0; e < 4; e++) mx = fmaxf(mx, v[e]);
+        for (int u = 0; u < 4; u++) {
+            const int g = g0 + u * kSampThreads + tid;
+            if (g < ngroups) load4(a, lrow, P, g * 4, v[u]);
+            else v[u][0] = v[u][1] = v[u][2] = v[u][3] = -INFINITY;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) mx = fmaxf(mx, v[u][e]);
     }
     mx = block_max(mx, S);
     const float inv_t = __fdiv_rn(1.0f, a.temperature);
     const float neg_m = -__fmul_rn(mx, inv_t);
 
-    // ---- pass 2: pinned sum of exp ----
-    float acc = 0.0f;
-    for (int g = tid; g < ngroups; g += kSampThreads) {
-        float v[4];
-        load_group(a, lrow, P, g, v);
+    // ---- pass 2: pinned sum of exp over the 1024 virtual threads ----
+    float acc_lo = 0.0f, acc_hi = 0.0f;
+    for (int g0 = 0; g0 < ngroups; g0 += kVirtThreads) {
+        const int ga = g0 + tid, gb = g0 + tid + kSampThreads;
+        float va[4], vb[4];
+        if (ga < ngroups) load4(a, lrow, P, ga * 4, va);
+        if (gb < ngroups) load4(a, lrow, P, gb * 4, vb);
+        if (ga < ngroups) {
 #pragma unroll
-        for (int e = 0; e < 4; e++)
-            if (g * 4 + e < a.vocab)
-                acc = __fadd_rn(acc, pinned_expf(__fadd_rn(__fmul_rn(v[e], inv_t), neg_m)));
+            for (int e = 0; e < 4; e++)
+                if (ga * 4 + e < a.vocab)
+                    acc_lo = __fadd_rn(acc_lo, pinned_expf_nonpos(__fadd_rn(__fmul_rn(va[e], inv_t), neg_m)));
+        }
+        if (gb < ngroups) {
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                if (gb * 4 + e < a.vocab)
+                    acc_hi = __fadd_rn(acc_hi, pinned_expf_nonpos(__fadd_rn(__fmul_rn(vb[e], inv_t), neg_m)));
+        }
     }
-    const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc, S));
+    const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
 
-    // ---- pass 3: exact parallel inverse-CDF scan ----
+    // ---- pass 3: exact parallel inverse-CDF scan over significant elements ----
     const float r = __ldg(a.uniforms + row);
+    if (!(r > 0.0f)) {  // cum >= r holds after the first element
+        if (tid == 0) a.out[row] = 0;
+        return;
+    }
     if (tid == 0) {
-        set_binade(S, 0.0f, r);
+        set_binade(S, 0.0f, r, inv);
         S.start = 0;
         S.result = -1;
     }
     __syncthreads();
-    const int ntiles = (ngroups + kSampThreads - 1) / kSampThreads;
+    float* cb = cbuf[w];
+    uint16_t* ci = cidx[w];
+    const int ntiles = (a.vocab + kTile - 1) / kTile;
     for (int tile = 0; tile < ntiles; tile++) {
-        const int g = tile * kSampThreads + tid;
-        float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        if (g < ngroups) {
-            float v[4];
-            load_group(a, lrow, P, g, v);
+        const int tbase = tile * kTile;
+        const int base = tbase + tid * kPerThread;
+        float d[kPerThread];
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                if (g * 4 + e < a.vocab)
-                    p[e] = __fmul_rn(pinned_expf(__fadd_rn(__fmul_rn(v[e], inv_t), neg_m)), inv);
+        for (int h = 0; h < kPerThread / 4; h++) {
+            float v[4];
+            load4(a, lrow, P, base + 4 * h, v);
+#pragma unroll
+            for (int e = 0; e < 4; e++) d[4 * h + e] = __fadd_rn(__fmul_rn(v[e], inv_t), neg_m);
         }
-        const int tile_end = min((tile + 1) * kSampThreads * 4, a.vocab);
+        // compact the significant elements of the warp, in element order
+        const float td0 = S.td;
+        uint32_t sig = 0;
+#pragma unroll
+        for (int e = 0; e < kPerThread; e++)
+            if (base + e < a.vocab && d[e] >= td0) sig |= 1u << e;
+        const int cnt = __popc(sig);
+        int incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += o;
+        }
+        const int nw = __shfl_sync(0xffffffffu, incl, 31);
+        int pos = incl - cnt;
+#pragma unroll
+        for (int e = 0; e < kPerThread; e++)
+            if ((sig >> e) & 1u) {
+                cb[pos] = d[e];
+                ci[pos] = (uint16_t)(tid * kPerThread + e);
+                pos++;
+            }
+        __syncwarp();
+        for (int j = lane; j < nw; j += kWarp) cb[j] = __fmul_rn(pinned_expf_nonpos(cb[j]), inv);
+        __syncwarp();
+        // lane l takes the contiguous items [l*c, l*c + c)
+        const int c = (nw + kWarp - 1) / kWarp;
+        const int first = lane * c;
+        const int mine = max(0, min(c, nw - first));
+        float pv[kPerThread];
+        int li[kPerThread];
+#pragma unroll
+        for (int q = 0; q < kPerThread; q++) {
+            pv[q] = q < mine ? cb[first + q] : 0.0f;
+            li[q] = q < mine ? (int)ci[first + q] : 0x7FFF;
+        }
+
+        const int tile_end = min(tbase + kTile, a.vocab);
         while (true) {
             const uint32_t ucum = S.ucum;
             const int E = S.E, start = S.start;
             const uint32_t tr = S.tr;
-            uint32_t k[4];
-            bool ser[4], valid[4];
+            uint32_t k[kPerThread];
+            bool ser[kPerThread], valid[kPerThread];
             uint32_t kt = 0;
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int i = g * 4 + e;
-                valid[e] = g < ngroups && i < a.vocab && i >= start;
-                bool tie, big;
-                classify(p[e], E, k[e], tie, big);
-                ser[e] = tie || big;
-                if (!valid[e]) { k[e] = 0; ser[e] = false; }
-                kt = sat_add(kt, ser[e] ? kSat : k[e]);
+            for (int q = 0; q < kPerThread; q++) {
+                k[q] = 0;
+                ser[q] = false;
+                valid[q] = false;
+                if (q < c) {  // warp-uniform: skip slots no lane holds
+                    valid[q] = q < mine && tbase + li[q] >= start;
+                    bool tie, big;
+                    classify(pv[q], E, k[q], tie, big);
+                    ser[q] = valid[q] && (tie || big);
+                    if (!valid[q]) k[q] = 0;
+                    kt = sat_add(kt, ser[q] ? kSat : k[q]);
+                }
             }
-            // block exclusive scan of kt (saturating)
             uint32_t inc = kt;
+#pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
                 const uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
                 if (lane >= off) inc = sat_add(inc, o);
             }
-            if (lane == 31) S.wscan[w] = inc;
+            if (lane == 31) S.wscan[w] = inc;  // warp total
             __syncthreads();
-            if (w == 0) {
-                uint32_t t = S.wscan[lane];
-                for (int off = 1; off < 32; off <<= 1) {
-                    const uint32_t o = __shfl_up_sync(0xffffffffu, t, off);
-                    if (lane >= off) t = sat_add(t, o);
-                }
-                S.red_u[lane] = t;  // inclusive warp-total scan
+            // prefix over the warp totals: lane j holds warp j's total
+            uint32_t wt = lane < kSampWarps ? S.wscan[lane] : 0u;
+#pragma unroll
+            for (int off = 1; off < kSampWarps; off <<= 1) {
+                const uint32_t o = __shfl_up_sync(0xffffffffu, wt, off);
+                if (lane >= off) wt = sat_add(wt, o);
             }
-            __syncthreads();
+            const uint32_t all = __shfl_sync(0xffffffffu, wt, kSampWarps - 1);
+            uint32_t wpre = __shfl_sync(0xffffffffu, wt, (w + 31) & 31);
+            if (w == 0) wpre = 0;
             uint32_t excl = __shfl_up_sync(0xffffffffu, inc, 1);
             if (lane == 0) excl = 0;
-            uint32_t run = sat_add(ucum, sat_add(w > 0 ? S.red_u[w - 1] : 0u, excl));
-            const uint32_t total = S.red_u[kSampWarps - 1];
-            // first event of this thread
-            uint32_t ev = kNoEvent;
-            uint32_t before = run;
+            uint32_t run = sat_add(ucum, sat_add(wpre, excl));
+            // first event of this lane: serial (tie / big / binade crossing) or hit
+            uint32_t ev = kNoEvent, before = run;
+            int evq = 0;
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                if (!valid[e] || ev != kNoEvent) continue;
-                const uint32_t local = (uint32_t)(tid * 4 + e);
-                if (ser[e]) { ev = local << 1; before = run; break; }
-                const uint32_t nr = sat_add(run, k[e]);
-                if (nr >= kBinadeUnits) { ev = local << 1; before = run; break; }
-                if (nr >= tr) { ev = (local << 1) | 1u; break; }
+            for (int q = 0; q < kPerThread; q++) {
+                if (q >= c) break;  // warp-uniform
+                if (!valid[q] || ev != kNoEvent) continue;
+                const uint32_t local = (uint32_t)li[q];
+                if (ser[q]) { ev = local << 1; before = run; evq = q; continue; }
+                const uint32_t nr = sat_add(run, k[q]);
+                if (nr >= kBinadeUnits) { ev = local << 1; before = run; evq = q; continue; }
+                if (nr >= tr) { ev = (local << 1) | 1u; evq = q; continue; }
                 run = nr;
             }
             const uint32_t wmin = __reduce_min_sync(0xffffffffu, ev);
-            if (lane == 0) S.wscan[w] = wmin;
+            if (lane == 0) S.red_u[w] = wmin;
             __syncthreads();
-            if (w == 0) {
-                const uint32_t m = __reduce_min_sync(0xffffffffu, S.wscan[lane]);
-                if (lane == 0) S.ev = m;
-            }
-            __syncthreads();
-            const uint32_t gev = S.ev;
+            const uint32_t gev =
+                __reduce_min_sync(0xffffffffu, lane < kSampWarps ? S.red_u[lane] : kNoEvent);
             if (gev == kNoEvent) {
                 if (tid == 0) {
-                    S.ucum = ucum + total;  // no crossing: exact and < 2^24
+                    S.ucum = ucum + all;  // no crossing: exact and < 2^24
                     S.start = tile_end;
                 }
                 __syncthreads();
                 break;
             }
-            const int local = (int)(gev >> 1);
             if (ev == gev) {  // owner of the first event
-                const int i = tile * kSampThreads * 4 + local;
+                const int i = tbase + (int)(gev >> 1);
                 if (gev & 1u) {
                     S.result = i;
                 } else {
-                    // exact running sum before element i, then a real fp32 add
-                    // before * 2^(E-23), exact: two power-of-two scalings
+                    float pe = pv[0];
+#pragma unroll
+                    for (int q = 1; q < kPerThread; q++)
+                        if (q == evq) pe = pv[q];
+                    // before * 2^(E-23), exact: two power-of-two scalings; then a real fp32 add
                     const float cum_prev =
                         __fmul_rn(__fmul_rn((float)before, pow2i(E - 23 + 64)), pow2i(-64));
-                    const float cum = __fadd_rn(cum_prev, p[local & 3]);
+                    const float cum = __fadd_rn(cum_prev, pe);
                     if (cum >= r) S.result = i;
-                    else { set_binade(S, cum, r); S.start = i + 1; }
+                    else { set_binade(S, cum, r, inv); S.start = i + 1; }
                 }
             }
             __syncthreads();
@@ -406,25 +499,34 @@ sample_rows_kernel(const SampArgs a) {
 }
 
 // softmax over rows in place (core/cpu_ops.cpp:83-99) with the pinned sum.
-__global__ void __launch_bounds__(kSampThreads, 1)
+__global__ void __launch_bounds__(kSampThreads, 2)
 softmax_rows_kernel(float* x, int n, int64_t stride) {
     __shared__ RowSmem S;
     float* row = x + (int64_t)blockIdx.x * stride;
+    const int tid = threadIdx.x;
     const int ngroups = (n + 3) >> 2;
     float mx = -INFINITY;
-    for (int g = threadIdx.x; g < ngroups; g += kSampThreads)
+    for (int g = tid; g < ngroups; g += kSampThreads)
         for (int e = 0; e < 4 && g * 4 + e < n; e++) mx = fmaxf(mx, row[g * 4 + e]);
     const float neg_m = -block_max(mx, S);
-    float acc = 0.0f;
-    for (int g = threadIdx.x; g < ngroups; g += kSampThreads)
-        for (int e = 0; e < 4 && g * 4 + e < n; e++) {
-            const float v = pinned_expf(__fadd_rn(row[g * 4 + e], neg_m));
-            row[g * 4 + e] = v;
-            acc = __fadd_rn(acc, v);
-        }
-    const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc, S));
-    for (int g = threadIdx.x; g < ngroups; g += kSampThreads)
-        for (int e = 0; e < 4 && g * 4 + e < n; e++) row[g * 4 + e] = __fmul_rn(row[g * 4 + e], inv);
+    float acc_lo = 0.0f, acc_hi = 0.0f;
+    for (int g0 = 0; g0 < ngroups; g0 += kVirtThreads) {
+        const int ga = g0 + tid, gb = g0 + tid + kSampThreads;
+        if (ga < ngroups)
+            for (int e = 0; e < 4 && ga * 4 + e < n; e++) {
+                const float v = pinned_expf_nonpos(__fadd_rn(row[ga * 4 + e], neg_m));
+                row[ga * 4 + e] = v;
+                acc_lo = __fadd_rn(acc_lo, v);
+            }
+        if (gb < ngroups)
+            for (int e = 0; e < 4 && gb * 4 + e < n; e++) {
+                const float v = pinned_expf_nonpos(__fadd_rn(row[gb * 4 + e], neg_m));
+                row[gb * 4 + e] = v;
+                acc_hi = __fadd_rn(acc_hi, v);
+            }
+    }
+    const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
+    for (int i = tid; i < n; i += kSampThreads) row[i] = __fmul_rn(row[i], inv);
 }
 
 }  // namespace ane
@@ -456,18 +558,18 @@ int ane_cuda_sample_rows(const float* logits, int64_t rows, int vocab, int64_t l
     int slots_log2 = 5;
     while ((1 << slots_log2) < 2 * window) slots_log2++;
     const size_t smem = (size_t)(1 << slots_log2) * 12 + (size_t)((vocab + 31) / 32) * 4;
-    if (smem > 200 * 1024) return fail(ANE_CUDA_ERR_UNSUPPORTED, "sample_rows: vocab %d too large", vocab);
-    static thread_local int configured_dev = -1;
-    static thread_local size_t configured_smem = 0;
+    constexpr size_t kMaxDyn = 180 * 1024;  // plus 16 KB of static shared memory
+    if (smem > kMaxDyn) return fail(ANE_CUDA_ERR_UNSUPPORTED, "sample_rows: vocab %d too large", vocab);
+    static int configured[64] = {0};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured_dev != dev || configured_smem < smem) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return fail(ANE_CUDA_ERR_CUDA, "sample_rows: no current device");
+    if (!configured[dev]) {
         cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDyn);
         if (e != cudaSuccess)
             return fail(ANE_CUDA_ERR_CUDA, "sample_rows: %s", cudaGetErrorString(e));
-        configured_dev = dev;
-        configured_smem = 200 * 1024;
+        configured[dev] = 1;
     }
     SampArgs a{logits, rows, vocab, logits_stride, history, history_len, history_stride, uniforms,
                temperature, repetition_penalty, frequency_penalty, repetition_context, out_tokens,
