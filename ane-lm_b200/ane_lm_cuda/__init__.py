@@ -42,6 +42,8 @@ _SIGS = {
     "ane_cuda_mul_sigmoid_inplace": (_i, [_i, _p, _p, _i64, _p]),
     "ane_cuda_softmax_rows": (_i, [_p, _i64, _i, _i64, _p]),
     "ane_cuda_sample_rows": (_i, [_p, _i64, _i, _i64, _p, _p, _i64, _p, _f, _f, _i, _f, _p, _p]),
+    "ane_cuda_write_ane_blobs": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
+    "ane_cuda_convert_model": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
 }
 
 _lib = None
@@ -187,6 +189,22 @@ def softmax_rows(x):
     rows, n = x.shape
     _check("softmax_rows", lib().ane_cuda_softmax_rows(_ptr(x), rows, n, x.stride(0), _stream(x)))
     return x
+
+
+def write_ane_blobs(safetensors_path: str, output_dir: str) -> int:
+    """`ane-lm convert` of one .safetensors file; returns the number of blobs."""
+    n = _i64(0)
+    _check("write_ane_blobs", lib().ane_cuda_write_ane_blobs(
+        safetensors_path.encode(), output_dir.encode(), C.byref(n), None))
+    return n.value
+
+
+def convert_model(model_dir: str, output_dir: str) -> int:
+    """`ane-lm convert` of a model directory (all shards); returns the blob count."""
+    n = _i64(0)
+    _check("convert_model", lib().ane_cuda_convert_model(
+        model_dir.encode(), output_dir.encode(), C.byref(n), None))
+    return n.value
 
 
 def sample_rows(logits, uniforms, history=None, history_len=None, temperature=0.6,

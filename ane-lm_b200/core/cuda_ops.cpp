@@ -89,7 +89,8 @@ int sample_token(const float* logits, int vocab_size, const SamplingParams& para
     float* d_u = reinterpret_cast<float*>(t_stage.dev + 16);
     int32_t* d_len = reinterpret_cast<int32_t*>(t_stage.dev + 32);
     int32_t* d_hist = reinterpret_cast<int32_t*>(t_stage.dev + 64);
-    const float r = (float)drand48();
+    // the reference draws only when it samples (core/sampling.cpp:45-58)
+    const float r = params.temperature > 0.0f ? (float)drand48() : 0.0f;
     const int32_t len = (int32_t)nh;
     cudaError_t e = cudaMemcpyAsync(d_u, &r, sizeof(r), cudaMemcpyHostToDevice, s);
     if (e == cudaSuccess) e = cudaMemcpyAsync(d_len, &len, sizeof(len), cudaMemcpyHostToDevice, s);

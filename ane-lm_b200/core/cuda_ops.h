@@ -56,8 +56,9 @@ struct SamplingParams {
 };
 
 // `logits` is a device pointer; `recent_tokens` is host memory, as in the
-// reference.  The uniform draw is (float)drand48(), as at
-// core/sampling.cpp:58, so srand48 seeds it.  Returns -1 on failure.
+// reference.  The uniform draw is (float)drand48(), taken only when
+// temperature > 0, as at core/sampling.cpp:58, so srand48 seeds the same
+// sequence.  Returns -1 on failure.
 int sample_token(const float* logits, int vocab_size, const SamplingParams& params,
                  const std::vector<int>& recent_tokens = {});
 

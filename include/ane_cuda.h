@@ -60,6 +60,26 @@ ANE_CUDA_API int ane_cuda_read_status_flags(uint32_t* flags, int clear);
  * (core/safetensors.cpp:335) and build_weight_blob (core/ane_runtime.cpp:207). */
 ANE_CUDA_API int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t n, void* stream);
 
+/* ---- `ane-lm convert` ----------------------------------------------------
+ * HOST paths, not device pointers.  The conversion runs on the calling
+ * thread's current device; staging (128 MiB pinned, 128 MiB device) is
+ * allocated per call.  Output files are byte-identical to the reference's.
+ *
+ * ane_cuda_write_ane_blobs replaces SafeTensors::write_ane_blobs
+ * (core/safetensors.cpp:345-383, blob format :316-343): every BF16 tensor of
+ * one .safetensors file becomes output_dir/<name with '.' -> '/'>.bin, a
+ * 128-byte header followed by the FP16 data; other dtypes are skipped.
+ * *written receives the number of blobs.
+ *
+ * ane_cuda_convert_model replaces ModelWeights::open + write_ane_blobs
+ * (core/model_loader.cpp:14-118, :163-171) as used by cmd_convert
+ * (main.cpp:169-192): shards from model.safetensors.index.json's weight_map
+ * (unique, sorted), else every *.safetensors below model_dir (sorted). */
+ANE_CUDA_API int ane_cuda_write_ane_blobs(const char* safetensors_path, const char* output_dir,
+                                          int64_t* written, void* stream);
+ANE_CUDA_API int ane_cuda_convert_model(const char* model_dir, const char* output_dir,
+                                        int64_t* written, void* stream);
+
 /* ---- embedding gather --------------------------------------------------
  * Replaces the row memcpy of Qwen3Model::forward (models/llm/qwen3.cpp:498),
  * batched: out[r, :] = table[ids[r], :].  out_dtype equals table_dtype (a

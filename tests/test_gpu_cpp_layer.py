@@ -1,0 +1,101 @@
+"""GPU: the reference-signature C++ layer (ane-lm_b200/core/cuda_ops.h), driven
+by a C++ program compiled here against the library, checked against the
+oracle -- the path a maintainer takes when dropping it into ANE-LM."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+
+pytestmark = pytest.mark.gpu
+TESTS = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(TESTS)
+PKG = os.path.join(REPO, "ane-lm_b200")
+CUDA = "/usr/local/cuda"
+
+
+def drand48_floats(seed, n):
+    """(float)drand48() after srand48(seed): the POSIX 48-bit LCG."""
+    x = ((seed & 0xFFFFFFFF) << 16) | 0x330E
+    out = []
+    for _ in range(n):
+        x = (0x5DEECE66D * x + 0xB) & ((1 << 48) - 1)
+        out.append(np.float32(x / float(1 << 48)))
+    return np.array(out, np.float32)
+
+
+@pytest.fixture(scope="module")
+def checker(ane, tmp_path_factory):
+    d = tmp_path_factory.mktemp("cpp")
+    exe = str(d / "cuda_ops_check")
+    subprocess.run(["g++", "-O2", "-std=c++17", os.path.join(TESTS, "cpp", "cuda_ops_check.cpp"),
+                    "-I", os.path.join(REPO, "include"), "-I", os.path.join(PKG, "core"),
+                    "-I", f"{CUDA}/include", "-L", PKG, "-lane_cuda", "-L", f"{CUDA}/lib64",
+                    "-lcudart", f"-Wl,-rpath,{PKG}", f"-Wl,-rpath,{CUDA}/lib64", "-o", exe],
+                   check=True)
+    return exe, d
+
+
+def test_reference_signature_layer(checker, oracle):
+    exe, d = checker
+    rng = np.random.default_rng(7)
+    dim, hd, nq, nkv, n, vocab = 2048, 128, 16, 8, 3072, 151936
+    x = rng.standard_normal(dim).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    qk = rng.standard_normal((nq + nkv) * hd).astype(np.float32)
+    cosr = np.cos(rng.uniform(0, 6, hd // 2)).astype(np.float32)
+    sinr = np.sin(rng.uniform(0, 6, hd // 2)).astype(np.float32)
+    g = (rng.standard_normal(n) * 4).astype(np.float32)
+    z = (rng.standard_normal(n) * 4).astype(np.float32)
+    logits = (rng.standard_normal(vocab) * 3).astype(np.float32)
+    hist = rng.integers(0, vocab, 300).astype(np.int32)
+    bf = rng.integers(0, 65536, 1000).astype(np.uint16)
+    inp, outp = d / "in.bin", d / "out.bin"
+    with open(inp, "wb") as f:
+        for a in (x, w, qk, cosr, sinr, g, z, logits, hist, bf):
+            f.write(a.tobytes())
+    subprocess.run([exe, str(inp), str(outp)], check=True, timeout=120)
+    raw = outp.read_bytes()
+    off = 0
+
+    def take(dtype, count):
+        nonlocal off
+        a = np.frombuffer(raw, dtype, count, off)
+        off += a.nbytes
+        return a
+
+    # rmsnorm in place: bit-exact with the oracle's fp32 rmsnorm
+    _, y = oracle.residual_rmsnorm(x[None], None, w)
+    assert np.array_equal(take(np.float32, dim), y[0])
+    # apply_rope_cached with caller tables: v0' = v0 c - v1 s, v1' = v1 c + v0 s
+    heads = qk.reshape(-1, hd)
+    a0, a1 = heads[:, :hd // 2], heads[:, hd // 2:]
+    want = np.concatenate([a0 * cosr - a1 * sinr, a1 * cosr + a0 * sinr], 1).ravel()
+    assert np.array_equal(take(np.float32, qk.size), want)
+    # no tables: cos/sin of the pinned sincos at the position, in registers
+    inv = oracle.rope_inv_freq(hd, 1e6)
+    sc = np.array([oracle.sincosf(np.float32(777) * f) for f in inv], np.float32)
+    s_, c_ = sc[:, 0], sc[:, 1]
+    want = np.concatenate([a0 * c_ - a1 * s_, a1 * c_ + a0 * s_], 1).ravel()
+    assert np.array_equal(take(np.float32, qk.size), want)
+    # silu_vec_inplace / mul_sigmoid_inplace (fp32: pinned exp, IEEE divide)
+    assert np.array_equal(take(np.float32, n), oracle.silu_mul(g[None], np.ones((1, n), np.float32))[0])
+    e = oracle.expf(-z)
+    assert np.array_equal(take(np.float32, n), g / (np.float32(1) + e))
+    # softmax
+    assert np.array_equal(take(np.float32, vocab), oracle.softmax_rows(logits[None])[0])
+    # sample_token: srand48(4242); four draws, greedy (no draw), one draw without history
+    u = drand48_floats(4242, 5)
+    toks = take(np.int32, 6)
+    for i in range(4):
+        assert toks[i] == oracle.sample_rows(logits[None], u[i:i + 1], hist[None],
+                                             np.array([300], np.int32))[0]
+    assert toks[4] == oracle.sample_rows(logits[None], u[:1], hist[None], np.array([300], np.int32),
+                                         temperature=0.0)[0]
+    assert toks[5] == oracle.sample_rows(logits[None], u[4:5])[0]
+    # bf16_to_f16_vec
+    assert np.array_equal(take(np.uint16, bf.size), oracle.bf16_to_f16(bf))
+    # a failing call reports through last_status() and the process carries on
+    assert take(np.int32, 1)[0] == 1
+    assert off == len(raw)
