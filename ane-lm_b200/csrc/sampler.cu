@@ -200,25 +200,27 @@ __device__ Penalty build_penalties(const SampArgs& a, int64_t row, const float* 
 }
 
 // p in units of U = 2^(E-23): k = round(p / U); tie when p / U is an exact
-// half; big when p >= 2^(E+1) (certain to leave the binade).
+// half; big when p >= 2^(E+1) (certain to leave the binade).  Branch-free:
+// p / U = m * 2^s; for s <= 0 the shift sh = min(-s, 31) leaves q = m >> sh
+// and a remainder rem; rounding to nearest adds 1 when rem > half, and
+// rem == half (sh > 0) is a tie.  sh >= 25 gives q = 0 and rem < half
+// because m < 2^24.
 __device__ __forceinline__ void classify(float p, int E, uint32_t& k, bool& tie, bool& big) {
     const uint32_t b = __float_as_uint(p);
-    const int pe = (int)((b >> 23) & 0xFFu);
-    const uint32_t m = pe ? ((b & 0x7FFFFFu) | 0x800000u) : (b & 0x7FFFFFu);
-    const int s = (pe ? pe : 1) - 127 - E;
-    k = 0; tie = false; big = false;
-    if (m == 0) return;
-    if (s >= 1) { big = true; return; }
-    if (s == 0) { k = m; return; }
-    const int sh = -s;
-    if (sh >= 25) return;
-    const uint32_t q = m >> sh, rem = m & ((1u << sh) - 1u), half = 1u << (sh - 1);
-    tie = rem == half;
+    const uint32_t pe = (b >> 23) & 0xFFu;
+    const uint32_t m = (b & 0x7FFFFFu) | (pe ? 0x800000u : 0u);
+    const int s = (int)(pe ? pe : 1u) - 127 - E;
+    big = m != 0u && s >= 1;
+    const uint32_t sh = (uint32_t)min(max(-s, 0), 31);
+    const uint32_t q = m >> sh;
+    const uint32_t rem = m & ((1u << sh) - 1u);
+    const uint32_t half = sh ? 1u << (sh - 1u) : 0u;
+    tie = sh != 0u && rem == half && m != 0u;
     k = q + (rem > half ? 1u : 0u);
 }
 
 // Sets the binade state of S from an exact fp32 running sum `cum`.
-__device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, float inv) {
+__device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, double ln_2inv) {
     const uint32_t b = __float_as_uint(cum);
     int e = (int)((b >> 23) & 0xFFu) - 127;
     if (e < -126) e = -126;
@@ -244,7 +246,8 @@ __device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, float
     // product's rounding (relative 2^-21) and for rounding td itself.  Below
     // U / 2 = 2^-126 a product near U / 2 would be subnormal and its rounding
     // no longer relative: no element is skipped there.
-    S.td = e - 24 >= -126 ? (float)(log(ldexp(1.0, e - 23) / (2.0 * (double)inv)) - 1e-4)
+    // ln(U / (2 inv)) = (E - 23) ln 2 - ln(2 inv), ln(2 inv) computed once per row
+    S.td = e - 24 >= -126 ? (float)((double)(e - 23) * 0.69314718055994530942 - ln_2inv - 1e-4)
                           : -INFINITY;
 }
 
@@ -346,8 +349,9 @@ sample_rows_kernel(const SampArgs a) {
         if (tid == 0) a.out[row] = 0;
         return;
     }
+    const double ln_2inv = log(2.0 * (double)inv);
     if (tid == 0) {
-        set_binade(S, 0.0f, r, inv);
+        set_binade(S, 0.0f, r, ln_2inv);
         S.start = 0;
         S.result = -1;
     }
@@ -415,9 +419,9 @@ sample_rows_kernel(const SampArgs a) {
             for (int q = 0; q < kPerThread; q++) {
                 k[q] = 0;
                 ser[q] = false;
-                valid[q] = false;
-                if (q < c) {  // warp-uniform: skip slots no lane holds
-                    valid[q] = q < mine && tbase + li[q] >= start;
+                valid[q] = q < c && q < mine && tbase + li[q] >= start;
+                // warp-uniform skip of slots that no lane holds any more
+                if (__any_sync(0xffffffffu, valid[q])) {
                     bool tie, big;
                     classify(pv[q], E, k[q], tie, big);
                     ser[q] = valid[q] && (tie || big);
@@ -487,7 +491,7 @@ sample_rows_kernel(const SampArgs a) {
                         __fmul_rn(__fmul_rn((float)before, pow2i(E - 23 + 64)), pow2i(-64));
                     const float cum = __fadd_rn(cum_prev, pe);
                     if (cum >= r) S.result = i;
-                    else { set_binade(S, cum, r, inv); S.start = i + 1; }
+                    else { set_binade(S, cum, r, ln_2inv); S.start = i + 1; }
                 }
             }
             __syncthreads();
