@@ -20,6 +20,8 @@ HEADER = os.path.join(REPO, "include", "ane_cuda.h")
 OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 F32, F16, BF16 = 0, 1, 2
 FLAG_BAD_TOKEN_ID = 0x1
+FLAG_BAD_CACHE = 0x2
+FLAG_WAIT_TIMEOUT = 0x4
 
 _p = C.c_void_p
 _i64 = C.c_int64
@@ -44,6 +46,9 @@ _SIGS = {
     "ane_cuda_sample_rows": (_i, [_p, _i64, _i, _i64, _p, _p, _i64, _p, _f, _f, _i, _f, _p, _p]),
     "ane_cuda_write_ane_blobs": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
     "ane_cuda_convert_model": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
+    "ane_cuda_decode_attention_workspace_size": (_i64, [_i64, _i, _i, _i, _i]),
+    "ane_cuda_decode_attention": (_i, [_i, _p, _i64, _p, _i64, _i, _p, _p, _i64, _p, _p, _i,
+                                       _i64, _i, _i, _i, _i, _p, _i64, _p]),
 }
 
 _lib = None
@@ -219,4 +224,33 @@ def sample_rows(logits, uniforms, history=None, history_len=None, temperature=0.
         _ptr(logits), rows, vocab, logits.stride(0), _ptr(history), _ptr(history_len), hs,
         _ptr(uniforms), temperature, repetition_penalty, repetition_context, frequency_penalty,
         _ptr(out), _stream(logits)))
+    return out
+
+
+def decode_attention_workspace_size(batch, n_heads, n_kv_heads, head_dim, max_len) -> int:
+    return int(lib().ane_cuda_decode_attention_workspace_size(batch, n_heads, n_kv_heads,
+                                                              head_dim, max_len))
+
+
+def decode_attention(q, k_cache, v_cache, cache_start, cache_len, max_len=None, out=None,
+                     workspace=None):
+    """q [batch, n_heads, head_dim]; k_cache, v_cache [batch, capacity, n_kv, head_dim];
+    cache_start, cache_len int32 [batch].  Returns out [batch, n_heads, head_dim].
+    workspace: a zero-filled uint8 tensor of decode_attention_workspace_size() bytes,
+    or None for the library-held one."""
+    torch = _torch()
+    _cuda(q, k_cache, v_cache, cache_start, cache_len, workspace)
+    batch, n_heads, head_dim = q.shape
+    _, capacity, n_kv, hd2 = k_cache.shape
+    if hd2 != head_dim or v_cache.shape != k_cache.shape:
+        raise ValueError("q / cache shapes disagree")
+    if max_len is None:
+        max_len = capacity
+    if out is None:
+        out = torch.empty_like(q)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check("decode_attention", lib().ane_cuda_decode_attention(
+        _dt(q), _ptr(out), out.stride(0), _ptr(q), q.stride(0), q.stride(1), _ptr(k_cache),
+        _ptr(v_cache), k_cache.stride(0), _ptr(cache_start), _ptr(cache_len), capacity, batch,
+        n_heads, n_kv, head_dim, max_len, _ptr(workspace), ws_bytes, _stream(q)))
     return out

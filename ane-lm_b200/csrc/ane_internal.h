@@ -26,6 +26,11 @@ inline bool valid_dtype(int dtype) {
     return dtype == ANE_CUDA_F32 || dtype == ANE_CUDA_F16 || dtype == ANE_CUDA_BF16;
 }
 
+// Device address of the current device's status word (the flags of
+// ane_cuda_read_status_flags), for kernels compiled in other files; NULL on
+// a CUDA error.
+unsigned int* status_flags_device();
+
 // Number of SMs of the current device (cached per device).
 int sm_count();
 

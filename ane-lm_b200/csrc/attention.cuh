@@ -1,0 +1,473 @@
+// attention.cuh -- decode attention over a ring KV cache, the kernel
+// (core/cpu_ops.cpp:173-240 gqa_attention; ring bookkeeping
+// models/llm/qwen3.cpp:475-488).
+//
+// One query token per sequence.  The keys of a sequence are cut into splits
+// of kAttnKeys; one CTA takes one (split, kv head, sequence) and serves all
+// the q heads of that kv head, so every K and V row is read from HBM once.
+// The CTA
+//   1. stages its K rows and V rows in shared memory with one bulk copy per
+//      row (TMA engine, 16-byte aligned rows; the ring wrap is per row),
+//      on two mbarriers so the score pass starts while V is in flight;
+//   2. computes the scores (a lane group per key, q in registers), the
+//      split's max, exp and sum, and its un-normalised P.V;
+//   3. with one split: writes the output; otherwise writes (m, l, o) to the
+//      workspace, and the CTA that finishes last for its (kv head,
+//      sequence) -- an atomic counter -- combines the splits and writes the
+//      output, then resets the counter to zero.
+// Every summation order is fixed, so a CPU restatement doing the same
+// operations in the same order reproduces the result bit for bit:
+//   dot   EPL = max(16 B / element, head_dim / 32) consecutive elements per
+//         lane, GL = head_dim / EPL lanes per key: an fmaf chain per lane,
+//         then an xor butterfly over the GL lanes;
+//   sum   local keys 0-31 and 32-63 each by a 32-lane butterfly, added;
+//   P.V   U = 4 warps x (32 / GL) key groups: group u takes keys u, u+U, ...
+//         (fmaf chain), a butterfly over the key groups of a warp, then the
+//         four warps added in order;
+//   merge M = max m_j, f_j = exp(m_j - M); O and L each as four fmaf chains
+//         over the splits j = w (mod 4), added in order; out = O * (1 / L).
+// exp is the pinned pinned_expf of ane_common.cuh.
+#pragma once
+
+#include "ane_common.cuh"
+#include "ane_internal.h"
+
+namespace ane {
+
+constexpr int kAttnKeys = 64;  // keys per split (per CTA)
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * kWarp;
+constexpr int kAttnMaxGroup = 8;  // q heads per kv head
+static_assert(kAttnThreads == 2 * kAttnKeys, "one copy-issuing thread per K row and per V row");
+
+struct AttnArgs {
+    void* out;
+    int64_t out_stride;  // elements between sequences; heads are head_dim apart
+    const void* q;
+    int64_t q_stride;
+    int q_head_stride;
+    const void* k_cache;  // [batch][capacity][n_kv][head_dim]
+    const void* v_cache;
+    int64_t cache_stride;  // elements between sequences
+    const int32_t* start;  // [batch] ring start
+    const int32_t* len;    // [batch] keys in the ring
+    int capacity;
+    int n_heads, n_kv;
+    int max_len, max_splits;
+    float scale;           // 1 / sqrtf(head_dim)
+    uint32_t* counters;    // [batch][n_kv], zero between calls
+    float* part_ml;        // [batch][n_heads][max_splits][2]
+    float* part_o;         // [batch][n_heads][max_splits][head_dim]
+    unsigned int* flags;   // device status word
+};
+
+template <typename T, int HD>
+struct AttnShape {
+    static constexpr int V = T::kVec;
+    static constexpr int EPL = HD / 32 > V ? HD / 32 : V;  // elements per lane
+    static constexpr int NV = EPL / V;                     // 16-byte vectors per lane
+    static constexpr int GL = HD / EPL;                    // lanes per key
+    static constexpr int KPW = kWarp / GL;                 // keys per warp step
+    static constexpr int U = kAttnWarps * KPW;             // key groups per CTA
+    static_assert(EPL % V == 0 && GL * EPL == HD && KPW * GL == kWarp, "head_dim layout");
+};
+
+// floats per key row of the probabilities in shared memory (vector loads)
+template <int G>
+__host__ __device__ constexpr int attn_prow() { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
+
+template <typename T, int HD, int G>
+constexpr size_t attn_smem_bytes() {
+    return 2 * (size_t)kAttnKeys * HD * sizeof(typename T::storage)  // K, V rows
+           + (size_t)kAttnKeys * attn_prow<G>() * sizeof(float)      // P, key-major
+           + (size_t)kAttnWarps * G * HD * sizeof(float);            // warp partials
+}
+
+// Dots of one 32-key block (keys kb*32 ..) with GC q heads held in registers.
+// The lanes of a key group (GL lanes, GL keys) hold partial dots of every
+// key of the group and reduce them by a reduce-scatter: at each stage of
+// the xor butterfly (offsets GL/2 .. 1) a lane keeps the half of the keys
+// matching its lane bit and adds the partner's partial for them, so lane l
+// ends with the full dot of key l of the group.  Each add pairs the same two
+// partial sums as the plain butterfly, so the result is the same, with
+// GL - 1 shuffles per head instead of GL * log2(GL).
+template <typename T, int HD, int GC>
+__device__ __forceinline__ void score_block(const typename T::storage* sK,
+                                            const float (&qf)[GC][AttnShape<T, HD>::EPL], int kb,
+                                            int lane, float (&dot)[GC]) {
+    using Sh = AttnShape<T, HD>;
+    constexpr int V = Sh::V, EPL = Sh::EPL, NV = Sh::NV, GL = Sh::GL, H2 = GL / 2;
+    const int l = lane % GL;
+    const typename T::storage* base = sK + (kb * kWarp + (lane / GL) * GL) * HD + l * EPL;
+    float v[H2][GC];
+    const bool up0 = (l & H2) != 0;
+#pragma unroll
+    for (int k = 0; k < H2; k++) {
+        float klo[EPL], khi[EPL];
+#pragma unroll
+        for (int c = 0; c < NV; c++) {
+            unpack<T>(*reinterpret_cast<const uint4*>(base + k * HD + c * V), &klo[c * V]);
+            unpack<T>(*reinterpret_cast<const uint4*>(base + (k + H2) * HD + c * V), &khi[c * V]);
+        }
+#pragma unroll
+        for (int g = 0; g < GC; g++) {
+            float plo = 0.0f, phi = 0.0f;
+#pragma unroll
+            for (int e = 0; e < EPL; e++) {
+                plo = __fmaf_rn(qf[g][e], klo[e], plo);
+                phi = __fmaf_rn(qf[g][e], khi[e], phi);
+            }
+            const float send = up0 ? plo : phi;
+            const float keep = up0 ? phi : plo;
+            v[k][g] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, H2));
+        }
+    }
+#pragma unroll
+    for (int off = H2 / 2; off >= 1; off >>= 1) {
+        const bool up = (l & off) != 0;
+#pragma unroll
+        for (int k = 0; k < off; k++) {
+#pragma unroll
+            for (int g = 0; g < GC; g++) {
+                const float send = up ? v[k][g] : v[k + off][g];
+                const float keep = up ? v[k + off][g] : v[k][g];
+                v[k][g] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < GC; g++) dot[g] = v[0][g];
+}
+
+template <typename T, int HD, int G>
+__global__ void __launch_bounds__(kAttnThreads)
+decode_attention_kernel(const AttnArgs a) {
+    using S = typename T::storage;
+    using Sh = AttnShape<T, HD>;
+    constexpr int V = Sh::V, EPL = Sh::EPL, NV = Sh::NV, GL = Sh::GL, KPW = Sh::KPW, U = Sh::U;
+    constexpr int PROW = attn_prow<G>();
+    constexpr int GA = (G + 1) / 2;  // heads of warps 0-1; warps 2-3 take the other G - GA
+    constexpr uint32_t ROW = HD * sizeof(S);
+    extern __shared__ __align__(16) unsigned char smem[];
+    S* const sK = reinterpret_cast<S*>(smem);
+    S* const sV = sK + kAttnKeys * HD;
+    float* const s_p = reinterpret_cast<float*>(sV + kAttnKeys * HD);  // [key][PROW]
+    float* const s_red = s_p + kAttnKeys * PROW;                      // [warp][G][HD]
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int64_t b = blockIdx.z;
+    const int len = __ldg(a.len + b), start = __ldg(a.start + b);
+    const int h0 = kvh * G;
+    S* const out = static_cast<S*>(a.out) + b * a.out_stride + (int64_t)h0 * HD;
+
+    const bool bad = len > a.capacity || len > a.max_len ||
+                     (len > 0 && (start < 0 || start >= a.capacity));
+    if (len <= 0 || bad) {  // core/cpu_ops.cpp:176-179: no keys -> zeros
+        if (split == 0) {
+            for (int i = tid; i < G * HD; i += kAttnThreads) out[i] = T::from_f(0.0f);
+            if (bad && tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_BAD_CACHE);
+        }
+        return;
+    }
+    const int nsplit = (len + kAttnKeys - 1) / kAttnKeys;
+    if (split >= nsplit) return;
+    const int t0 = split * kAttnKeys;
+    const int n = min(kAttnKeys, len - t0);
+
+    // ---- 1. stage K and V rows -------------------------------------------
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        mbar_expect_tx(&bars[0], (uint32_t)n * ROW);
+        mbar_expect_tx(&bars[1], (uint32_t)n * ROW);
+    }
+    __syncthreads();  // byte counts registered before any copy is issued
+    {
+        const int i = tid & (kAttnKeys - 1);  // threads 0-63 copy K rows, 64-127 V rows
+        if (i < n) {
+            int slot = start + t0 + i;  // ring position (models/llm/qwen3.cpp:190-204)
+            if (slot >= a.capacity) slot -= a.capacity;
+            const int64_t off = b * a.cache_stride + ((int64_t)slot * a.n_kv + kvh) * HD;
+            if (tid < kAttnKeys)
+                bulk_load(sK + i * HD, static_cast<const S*>(a.k_cache) + off, ROW, &bars[0]);
+            else
+                bulk_load(sV + i * HD, static_cast<const S*>(a.v_cache) + off, ROW, &bars[1]);
+        }
+    }
+
+    // Warp w scores keys kb*32 .. kb*32+31 (kb = w & 1) for the heads
+    // g0 .. g0+gc-1 (warps 2-3 the second half; with G odd they carry one
+    // unused head).  q is loaded while the copies fly.
+    const int kb = w & 1;
+    const int g0 = (w >> 1) * GA, gc = (w >> 1) ? G - GA : GA;
+    float qf[GA][EPL];
+#pragma unroll
+    for (int g = 0; g < GA; g++) {
+        const int h = h0 + min(g0 + g, G - 1);
+        const S* qp = static_cast<const S*>(a.q) + b * a.q_stride + (int64_t)h * a.q_head_stride +
+                      (lane % GL) * EPL;
+#pragma unroll
+        for (int c = 0; c < NV; c++) unpack<T>(ld_keep(qp + c * V), &qf[g][c * V]);
+    }
+
+    if (!__syncthreads_and(mbar_wait_bounded(&bars[0], 0))) {
+        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+        return;
+    }
+
+    // ---- 2a. scores, split max / exp / sum (lane = key within the block) ---
+    const int i = kb * kWarp + lane;  // this lane's key in the split
+    float x[GA];
+    {
+        float dot[GA];
+        score_block<T, HD, GA>(sK, qf, kb, lane, dot);
+#pragma unroll
+        for (int g = 0; g < GA; g++) {
+            x[g] = i < n ? __fmul_rn(dot[g], a.scale) : -INFINITY;
+            float mx = x[g];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            if (lane == 0 && g < gc) s_m[g0 + g][kb] = mx;
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < GA; g++) {
+        if (g < gc) {  // warp-uniform
+            const float m = fmaxf(s_m[g0 + g][0], s_m[g0 + g][1]);
+            const float e = i < n ? pinned_expf(__fsub_rn(x[g], m)) : 0.0f;
+            const float sum = butterfly_sum(e, kWarp);
+            if (lane == 0) s_l[g0 + g][kb] = sum;
+            s_p[i * PROW + g0 + g] = e;
+        }
+    }
+    if (!__syncthreads_and(mbar_wait_bounded(&bars[1], 0))) {
+        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+        return;
+    }
+
+    // ---- 2b. un-normalised P.V: key group u takes keys u, u+U, ... -------
+    const int j = lane / GL, l = lane % GL;
+    const int u = w * KPW + j;
+    float acc[G][EPL];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
+    for (int k = u; k < n; k += U) {
+        float vf[EPL];
+#pragma unroll
+        for (int c = 0; c < NV; c++)
+            unpack<T>(*reinterpret_cast<const uint4*>(sV + k * HD + l * EPL + c * V), &vf[c * V]);
+        float p[PROW];
+        if constexpr (PROW >= 4) {
+#pragma unroll
+            for (int c = 0; c < PROW / 4; c++) {
+                const float4 t = reinterpret_cast<const float4*>(s_p + k * PROW)[c];
+                p[4 * c] = t.x; p[4 * c + 1] = t.y; p[4 * c + 2] = t.z; p[4 * c + 3] = t.w;
+            }
+        } else if constexpr (PROW == 2) {
+            const float2 t = reinterpret_cast<const float2*>(s_p + k * PROW)[0];
+            p[0] = t.x; p[1] = t.y;
+        } else {
+            p[0] = s_p[k];
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int e = 0; e < EPL; e++) acc[g][e] = __fmaf_rn(p[g], vf[e], acc[g][e]);
+    }
+#pragma unroll
+    for (int off = kWarp / 2; off >= GL; off >>= 1) {
+#pragma unroll
+        for (int g = 0; g < G; g++)
+#pragma unroll
+            for (int e = 0; e < EPL; e++)
+                acc[g][e] = __fadd_rn(acc[g][e], __shfl_xor_sync(0xffffffffu, acc[g][e], off));
+    }
+    if (j == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float4* dst = reinterpret_cast<float4*>(s_red + (w * G + g) * HD + l * EPL);
+#pragma unroll
+            for (int e = 0; e < EPL / 4; e++)
+                dst[e] = make_float4(acc[g][4 * e], acc[g][4 * e + 1], acc[g][4 * e + 2], acc[g][4 * e + 3]);
+        }
+    }
+    __syncthreads();
+
+    // the split's o = ((R0 + R1) + R2) + R3 over the warps (or, in the
+    // merge, over the four chains)
+    auto sum4 = [&](int g, int d) {
+        const float* r = s_red + g * HD + d;
+        return __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[G * HD]), r[2 * G * HD]), r[3 * G * HD]);
+    };
+
+    if (nsplit == 1) {
+        // the merge below with one split: f = exp(m - m), chains 1-3 empty
+        for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
+            const int g = idx / HD, d = idx % HD;
+            const float m = fmaxf(s_m[g][0], s_m[g][1]);
+            const float f = pinned_expf(__fsub_rn(m, m));
+            const float lsum = __fadd_rn(s_l[g][0], s_l[g][1]);
+            const float L = __fadd_rn(__fadd_rn(__fadd_rn(__fmaf_rn(lsum, f, 0.0f), 0.0f), 0.0f), 0.0f);
+            const float O = __fadd_rn(__fadd_rn(__fadd_rn(__fmaf_rn(sum4(g, d), f, 0.0f), 0.0f), 0.0f), 0.0f);
+            out[idx] = T::from_f(__fmul_rn(O, __fdiv_rn(1.0f, L)));
+        }
+        return;
+    }
+
+    const int64_t pbase = (b * a.n_heads + h0) * (int64_t)a.max_splits;  // (seq, head h0, split 0)
+    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
+        const int g = idx / HD, d = idx % HD;
+        a.part_o[(pbase + (int64_t)g * a.max_splits + split) * HD + d] = sum4(g, d);
+    }
+    if (tid < G) {
+        float* ml = a.part_ml + (pbase + (int64_t)tid * a.max_splits + split) * 2;
+        ml[0] = fmaxf(s_m[tid][0], s_m[tid][1]);
+        ml[1] = __fadd_rn(s_l[tid][0], s_l[tid][1]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(a.counters + b * a.n_kv + kvh, 1u);
+        s_last = prev == (uint32_t)(nsplit - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid == 0) a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
+
+    // ---- 3. merge the splits (last CTA of this kv head and sequence) -------
+    for (int g = w; g < G; g += kAttnWarps) {
+        const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
+        float mx = -INFINITY;
+        for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, __ldcg(ml + 2 * s));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (lane == 0) s_M[g] = mx;
+    }
+    // f_j = exp(m_j - M) in tiles of FT splits over the K / V rows (no longer
+    // needed); O and L as four chains over j = c4 (mod 4), in order of j.
+    constexpr int FT = (int)((2 * (size_t)kAttnKeys * HD * sizeof(S) / sizeof(float)) / G) & ~3;
+    constexpr int COLS = HD / 4;
+    constexpr int ITEMS = G * 4 * COLS;  // (g, chain, float4 column)
+    constexpr int IPT = (ITEMS + kAttnThreads - 1) / kAttnThreads;
+    float* const s_f = reinterpret_cast<float*>(smem);  // [G][FT]
+    float4 o[IPT];
+#pragma unroll
+    for (int it = 0; it < IPT; it++) o[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float Lc = 0.0f;
+    for (int s0 = 0; s0 < nsplit; s0 += FT) {
+        const int s1 = min(nsplit, s0 + FT), ns = s1 - s0;
+        __syncthreads();  // s_M ready / the previous tile consumed
+        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
+            const int g = idx / ns, s = s0 + idx % ns;
+            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
+            s_f[g * FT + (s - s0)] = pinned_expf(__fsub_rn(__ldcg(ml + 2 * s), s_M[g]));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < IPT; it++) {
+            const int idx = tid + it * kAttnThreads;
+            if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
+                const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
+                const float4* po =
+                    reinterpret_cast<const float4*>(a.part_o + (pbase + (int64_t)g * a.max_splits) * HD) + col;
+                const float* f = s_f + g * FT;
+#pragma unroll 8
+                for (int s = s0 + c4; s < s1; s += 4) {
+                    const float4 v = __ldcg(po + (int64_t)s * COLS);
+                    const float fs = f[s - s0];
+                    o[it].x = __fmaf_rn(v.x, fs, o[it].x);
+                    o[it].y = __fmaf_rn(v.y, fs, o[it].y);
+                    o[it].z = __fmaf_rn(v.z, fs, o[it].z);
+                    o[it].w = __fmaf_rn(v.w, fs, o[it].w);
+                }
+            }
+        }
+        if (tid < 4 * G) {
+            const int c4 = tid & 3, g = tid >> 2;
+            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
+            const float* f = s_f + g * FT;
+#pragma unroll 8
+            for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(__ldcg(ml + 2 * s + 1), f[s - s0], Lc);
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < IPT; it++) {
+        const int idx = tid + it * kAttnThreads;
+        if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
+            const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
+            reinterpret_cast<float4*>(s_red + (c4 * G + g) * HD)[col] = o[it];
+        }
+    }
+    if (tid < 4 * G) s_L[tid >> 2][tid & 3] = Lc;
+    __syncthreads();
+    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
+        const int g = idx / HD, d = idx % HD;
+        const float L = __fadd_rn(__fadd_rn(__fadd_rn(s_L[g][0], s_L[g][1]), s_L[g][2]), s_L[g][3]);
+        out[idx] = T::from_f(__fmul_rn(sum4(g, d), __fdiv_rn(1.0f, L)));
+    }
+}
+
+
+// Launches the kernel instance for (head_dim, group); ANE_CUDA_ERR_UNSUPPORTED
+// for shapes without one.
+template <typename T>
+int launch_decode_attention(const AttnArgs& a, int head_dim, int group, int64_t batch,
+                            cudaStream_t s);
+
+}  // namespace ane
+
+namespace ane {
+
+template <typename T, int HD, int G>
+int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
+    constexpr size_t smem = attn_smem_bytes<T, HD, G>();
+    auto kern = decode_attention_kernel<T, HD, G>;
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess)
+            return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
+    }
+    const dim3 grid((unsigned)a.max_splits, (unsigned)a.n_kv, (unsigned)batch);
+    kern<<<grid, kAttnThreads, smem, s>>>(a);
+    return check_launch("decode_attention");
+}
+
+template <typename T, int HD>
+int launch_attention_hd(const AttnArgs& a, int group, int64_t batch, cudaStream_t s) {
+    switch (group) {
+        case 1: return launch_attention_shape<T, HD, 1>(a, batch, s);
+        case 2: return launch_attention_shape<T, HD, 2>(a, batch, s);
+        case 3: return launch_attention_shape<T, HD, 3>(a, batch, s);
+        case 4: return launch_attention_shape<T, HD, 4>(a, batch, s);
+        case 5: return launch_attention_shape<T, HD, 5>(a, batch, s);
+        case 6: return launch_attention_shape<T, HD, 6>(a, batch, s);
+        case 7: return launch_attention_shape<T, HD, 7>(a, batch, s);
+        case 8: return launch_attention_shape<T, HD, 8>(a, batch, s);
+        default: return fail(ANE_CUDA_ERR_UNSUPPORTED, "decode_attention: %d q heads per kv head", group);
+    }
+}
+
+template <typename T>
+int launch_decode_attention(const AttnArgs& a, int head_dim, int group, int64_t batch,
+                            cudaStream_t s) {
+    switch (head_dim) {
+        case 64: return launch_attention_hd<T, 64>(a, group, batch, s);
+        case 128: return launch_attention_hd<T, 128>(a, group, batch, s);
+        case 256: return launch_attention_hd<T, 256>(a, group, batch, s);
+        default: return fail(ANE_CUDA_ERR_UNSUPPORTED, "decode_attention: head_dim %d", head_dim);
+    }
+}
+
+}  // namespace ane

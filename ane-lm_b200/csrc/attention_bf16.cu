@@ -1,0 +1,7 @@
+// attention_bf16.cu -- the BF16 instances of the decode-attention kernel
+// (compiled apart so the three element types build in parallel).
+#include "attention.cuh"
+
+namespace ane {
+template int launch_decode_attention<BF16>(const AttnArgs&, int, int, int64_t, cudaStream_t);
+}  // namespace ane

@@ -59,6 +59,18 @@ gather_elem_kernel(typename TO::storage* __restrict__ out,
     for (int c = lane; c < hidden; c += kWarp) o[c] = TO::from_f(TI::to_f(t[c]));
 }
 
+unsigned int* status_flags_device() {
+    static unsigned int* addr[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_status_flags) != cudaSuccess) return nullptr;
+        addr[dev] = static_cast<unsigned int*>(p);
+    }
+    return addr[dev];
+}
+
 }  // namespace ane
 
 extern "C" {

@@ -43,6 +43,8 @@ typedef enum { ANE_CUDA_F32 = 0, ANE_CUDA_F16 = 1, ANE_CUDA_BF16 = 2 } ane_cuda_
 
 /* bits of the per-device status word */
 #define ANE_CUDA_FLAG_BAD_TOKEN_ID 0x1u /* a gather id was outside [0, vocab) */
+#define ANE_CUDA_FLAG_BAD_CACHE    0x2u /* a KV ring start / len outside the cache */
+#define ANE_CUDA_FLAG_WAIT_TIMEOUT 0x4u /* a kernel gave up waiting on its own copies */
 
 ANE_CUDA_API int ane_cuda_abi_version(void);
 ANE_CUDA_API const char* ane_cuda_status_string(int status);
@@ -162,6 +164,39 @@ ANE_CUDA_API int ane_cuda_sample_rows(const float* logits, int64_t rows, int voc
                          int64_t history_stride, const float* uniforms, float temperature,
                          float repetition_penalty, int repetition_context,
                          float frequency_penalty, int32_t* out_tokens, void* stream);
+
+/* ---- decode attention over a ring KV cache ----------------------------
+ * Replaces gqa_attention (core/cpu_ops.cpp:173-240, declared at
+ * core/cpu_ops.h:55-58) for `batch` sequences of one query token each.
+ * Sequence b: q heads at q + b*q_stride + h*q_head_stride; its cache rows
+ * [capacity][n_kv_heads][head_dim] at k_cache / v_cache + b*cache_stride;
+ * the cache_len[b] keys start at slot cache_start[b] and wrap at
+ * cache_capacity (models/llm/qwen3.cpp:475-488).  q head h reads kv head
+ * h / (n_heads / n_kv_heads).  out + b*out_stride + h*head_dim receives
+ * softmax(q.k / sqrtf(head_dim)) . v, zeros when cache_len[b] <= 0.
+ * A (start, len) outside the cache, or len > max_len, writes zeros and
+ * sets ANE_CUDA_FLAG_BAD_CACHE.  max_len bounds every cache_len[b] and
+ * sizes the launch.  fp32 arithmetic; the reference's softmax-weighted sum
+ * with its sums taken in a fixed parallel order (within 1e-6 x max|v| of
+ * the reference in fp32).
+ * head_dim 64, 128 or 256; at most 8 q heads per kv head; q and the caches
+ * 16-byte aligned with strides that keep rows 16-byte aligned.
+ * Workspace: ane_cuda_decode_attention_workspace_size() bytes (0 when
+ * max_len <= 64), 256-byte aligned, zero-filled before its first use (calls
+ * leave it zeroed); calls that share one must be ordered on one stream.
+ * workspace == NULL uses a buffer the library allocates per device and
+ * stream on first use and keeps. */
+ANE_CUDA_API int64_t ane_cuda_decode_attention_workspace_size(int64_t batch, int n_heads,
+                                                              int n_kv_heads, int head_dim,
+                                                              int max_len);
+ANE_CUDA_API int ane_cuda_decode_attention(int dtype, void* out, int64_t out_stride, const void* q,
+                                           int64_t q_stride, int q_head_stride,
+                                           const void* k_cache, const void* v_cache,
+                                           int64_t cache_stride, const int32_t* cache_start,
+                                           const int32_t* cache_len, int cache_capacity,
+                                           int64_t batch, int n_heads, int n_kv_heads,
+                                           int head_dim, int max_len, void* workspace,
+                                           int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

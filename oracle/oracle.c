@@ -373,6 +373,165 @@ void or_softmax_rows(float* x, int64_t rows, int n, int64_t stride) {
 }
 
 /* ------------------------------------------------------------------ */
+/* Decode attention over a ring KV cache, core/cpu_ops.cpp:173-240      */
+/* ------------------------------------------------------------------ */
+
+/* xor butterfly over n values (offsets n/2 .. 1); every slot ends equal. */
+static float butterfly(float* a, int n) {
+    float nx[64];
+    for (int off = n >> 1; off >= 1; off >>= 1) {
+        for (int l = 0; l < n; l++) nx[l] = a[l] + a[l ^ off];
+        memcpy(a, nx, (size_t)n * sizeof(float));
+    }
+    return a[0];
+}
+
+/* One query token per sequence against its ring cache.  The reference
+ * (core/cpu_ops.cpp:173-240) computes, per q head h of kv head h / groups,
+ *   s_t = dot(q_h, k_t) * (1/sqrtf(head_dim)),   t over the cache_len
+ *         slots from cache_start, wrapping at cache_capacity (:188-205);
+ *   p   = softmax(s) (:207, core/cpu_ops.cpp:83-99);
+ *   out = sum_t p_t v_t (:209-219);
+ * and zeros when cache_len <= 0 (:176-179).  The summation orders are
+ * pinned here (the CUDA kernel does the same operations in the same order):
+ *   - dot: EPL = max(16 / element size, head_dim / 32) consecutive elements
+ *     per lane, GL = head_dim / EPL lanes; each lane an fmaf chain over its
+ *     elements; xor butterfly over the GL lane sums.
+ *   - keys in splits of 64; per split j: m_j = max s, e_t = expf(s_t - m_j),
+ *     l_j = two 32-lane butterflies (local keys 0-31, 32-63) added;
+ *     o_j[d] = U = 4 * (32 / GL) accumulators, accumulator u an fmaf chain
+ *     over local keys u, u+U, ...; xor butterfly over each warp's 32/GL
+ *     accumulators; the four warp results added in order.
+ *   - combine: M = max m_j, f_j = expf(m_j - M); O[d] and L each as four
+ *     fmaf chains over splits j = w mod 4, added in order; out = O * (1/L).
+ * The result is the reference's softmax-weighted sum with the
+ * normalisation applied once at the end (the split-softmax identity). */
+#define OR_ATTN_KEYS 64
+void or_decode_attention(int dt, void* out, int64_t out_stride,
+                         const void* q, int64_t q_stride, int q_head_stride,
+                         const void* k_cache, const void* v_cache, int64_t cache_stride,
+                         const int32_t* cache_start, const int32_t* cache_len, int capacity,
+                         int64_t batch, int n_heads, int n_kv_heads, int head_dim) {
+    const int es = dt == OR_F32 ? 4 : 2;
+    const int epl = (head_dim / 32 > 16 / es) ? head_dim / 32 : 16 / es;
+    const int gl = head_dim / epl;
+    const int kpw = 32 / gl;
+    const int U = 4 * kpw;
+    const int groups = n_heads / n_kv_heads;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    const int64_t kv_step = (int64_t)n_kv_heads * head_dim;
+    float* qf = (float*)malloc((size_t)head_dim * sizeof(float));
+    float* kbuf = (float*)malloc((size_t)OR_ATTN_KEYS * head_dim * sizeof(float));
+    float* vbuf = (float*)malloc((size_t)OR_ATTN_KEYS * head_dim * sizeof(float));
+    float* acc = (float*)malloc((size_t)U * head_dim * sizeof(float));
+    float* O = (float*)malloc((size_t)4 * head_dim * sizeof(float));
+    for (int64_t b = 0; b < batch; b++) {
+        const int len = cache_len[b], start = cache_start[b];
+        const int nsplit = len > 0 ? (len + OR_ATTN_KEYS - 1) / OR_ATTN_KEYS : 0;
+        float* pm = (float*)malloc((size_t)(nsplit ? nsplit : 1) * sizeof(float));
+        float* pl = (float*)malloc((size_t)(nsplit ? nsplit : 1) * sizeof(float));
+        float* po = (float*)malloc((size_t)(nsplit ? nsplit : 1) * head_dim * sizeof(float));
+        for (int h = 0; h < n_heads; h++) {
+            const int kvh = h / groups;
+            for (int d = 0; d < head_dim; d++)
+                qf[d] = ld(q, dt, b * q_stride + (int64_t)h * q_head_stride + d);
+            if (len <= 0) {
+                for (int d = 0; d < head_dim; d++) st(out, dt, b * out_stride + (int64_t)h * head_dim + d, 0.0f);
+                continue;
+            }
+            for (int j = 0; j < nsplit; j++) {
+                const int t0 = j * OR_ATTN_KEYS;
+                const int n = len - t0 < OR_ATTN_KEYS ? len - t0 : OR_ATTN_KEYS;
+                float s[OR_ATTN_KEYS], e[OR_ATTN_KEYS];
+                for (int i = 0; i < n; i++) {
+                    int slot = start + t0 + i;
+                    if (slot >= capacity) slot -= capacity;
+                    const int64_t off = b * cache_stride + (int64_t)slot * kv_step + (int64_t)kvh * head_dim;
+                    for (int d = 0; d < head_dim; d++) {
+                        kbuf[i * head_dim + d] = ld(k_cache, dt, off + d);
+                        vbuf[i * head_dim + d] = ld(v_cache, dt, off + d);
+                    }
+                    float lanes[32];
+                    for (int l = 0; l < gl; l++) {
+                        float a = 0.0f;
+                        for (int x = 0; x < epl; x++)
+                            a = fmaf(qf[l * epl + x], kbuf[i * head_dim + l * epl + x], a);
+                        lanes[l] = a;
+                    }
+                    s[i] = butterfly(lanes, gl) * scale;
+                }
+                float m = -INFINITY;
+                for (int i = 0; i < n; i++) m = fmaxf(m, s[i]);
+                float w32[2][32];
+                for (int i = 0; i < OR_ATTN_KEYS; i++) {
+                    e[i] = i < n ? or_expf(s[i] - m) : 0.0f;
+                    w32[i / 32][i % 32] = e[i];
+                }
+                const float l0 = butterfly(w32[0], 32), l1 = butterfly(w32[1], 32);
+                pm[j] = m;
+                pl[j] = l0 + l1;
+                for (int u = 0; u < U; u++) {
+                    for (int d = 0; d < head_dim; d++) {
+                        float a = 0.0f;
+                        for (int i = u; i < n; i += U) a = fmaf(e[i], vbuf[i * head_dim + d], a);
+                        acc[u * head_dim + d] = a;
+                    }
+                }
+                for (int d = 0; d < head_dim; d++) {
+                    float r[4];
+                    for (int w = 0; w < 4; w++) {
+                        float g[32];
+                        for (int x = 0; x < kpw; x++) g[x] = acc[(w * kpw + x) * head_dim + d];
+                        r[w] = butterfly(g, kpw);
+                    }
+                    po[(int64_t)j * head_dim + d] = ((r[0] + r[1]) + r[2]) + r[3];
+                }
+            }
+            float M = -INFINITY;
+            for (int j = 0; j < nsplit; j++) M = fmaxf(M, pm[j]);
+            float L[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int d = 0; d < 4 * head_dim; d++) O[d] = 0.0f;
+            for (int j = 0; j < nsplit; j++) {
+                const float f = or_expf(pm[j] - M);
+                const int w = j & 3;
+                L[w] = fmaf(pl[j], f, L[w]);
+                for (int d = 0; d < head_dim; d++)
+                    O[w * head_dim + d] = fmaf(po[(int64_t)j * head_dim + d], f, O[w * head_dim + d]);
+            }
+            const float inv = 1.0f / (((L[0] + L[1]) + L[2]) + L[3]);
+            for (int d = 0; d < head_dim; d++) {
+                const float o = ((O[d] + O[head_dim + d]) + O[2 * head_dim + d]) + O[3 * head_dim + d];
+                st(out, dt, b * out_stride + (int64_t)h * head_dim + d, o * inv);
+            }
+        }
+        free(pm);
+        free(pl);
+        free(po);
+    }
+    free(qf);
+    free(kbuf);
+    free(vbuf);
+    free(acc);
+    free(O);
+}
+
+/* models/llm/qwen3.cpp:475-484: append while the ring has room, else
+ * overwrite the oldest slot and advance the start. */
+int or_kv_ring_advance(int32_t* start, int32_t* len, int capacity) {
+    int slot;
+    if (*len < capacity) {
+        slot = *start + *len;
+        if (slot >= capacity) slot -= capacity;
+        (*len)++;
+    } else {
+        slot = *start;
+        (*start)++;
+        if (*start >= capacity) *start = 0;
+    }
+    return slot;
+}
+
+/* ------------------------------------------------------------------ */
 /* Sampler, core/sampling.cpp:10-66 and softmax core/cpu_ops.cpp:83-99  */
 /* ------------------------------------------------------------------ */
 static int32_t sample_one(const float* logits, int vocab, const int32_t* hist,

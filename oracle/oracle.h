@@ -85,6 +85,17 @@ int64_t or_embedding_gather(void* out, int out_dtype, const void* table,
 
 void or_softmax_rows(float* x, int64_t rows, int n, int64_t stride);
 
+/* ---- decode attention (core/cpu_ops.cpp:173-240) ---- */
+void or_decode_attention(int dtype, void* out, int64_t out_stride,
+                         const void* q, int64_t q_stride, int q_head_stride,
+                         const void* k_cache, const void* v_cache, int64_t cache_stride,
+                         const int32_t* cache_start, const int32_t* cache_len, int capacity,
+                         int64_t batch, int n_heads, int n_kv_heads, int head_dim);
+
+/* KV ring bookkeeping of models/llm/qwen3.cpp:475-484: the slot the new
+ * token goes to; start / len updated in place. */
+int or_kv_ring_advance(int32_t* start, int32_t* len, int capacity);
+
 /* ---- sampler ---- */
 void or_sample_rows(const float* logits, int64_t rows, int vocab,
                     int64_t logits_stride,

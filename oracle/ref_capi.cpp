@@ -80,6 +80,14 @@ int ref_sample_token(const float* logits, int vocab, float temperature, float re
     return tok;
 }
 
+/* gqa_attention (core/cpu_ops.cpp:173-240) for one query token. */
+void ref_gqa_attention(float* out, const float* q, const float* k_cache, const float* v_cache,
+                       int n_heads, int n_kv_heads, int head_dim, int q_head_stride,
+                       int cache_start, int cache_len, int cache_capacity) {
+    ane_lm::gqa_attention(out, q, k_cache, v_cache, n_heads, n_kv_heads, head_dim, q_head_stride,
+                          cache_start, cache_len, cache_capacity);
+}
+
 /* `ane-lm convert` for one safetensors file: SafeTensors::open followed by
  * SafeTensors::write_ane_blobs (core/safetensors.cpp:203-245, :345-383). */
 int ref_write_ane_blobs(const char* safetensors_path, const char* out_dir) {

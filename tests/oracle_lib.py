@@ -61,6 +61,10 @@ def load_oracle() -> C.CDLL:
     lib.or_softmax_rows.argtypes = [_p, _i64, C.c_int, _i64]
     lib.or_sample_rows.argtypes = [_p, _i64, C.c_int, _i64, _p, _p, _i64, _p, _f, _f,
                                    C.c_int, _f, _p]
+    lib.or_decode_attention.argtypes = [C.c_int, _p, _i64, _p, _i64, C.c_int, _p, _p, _i64,
+                                        _p, _p, C.c_int, _i64, C.c_int, C.c_int, C.c_int]
+    lib.or_kv_ring_advance.restype = C.c_int
+    lib.or_kv_ring_advance.argtypes = [_p, _p, C.c_int]
     return lib
 
 
@@ -76,6 +80,8 @@ def load_ref():
     lib.ref_rope_row.argtypes = [_p, _p, C.c_int, C.c_int, _f]
     lib.ref_silu_vec_inplace.argtypes = [_p, C.c_int]
     lib.ref_softmax.argtypes = [_p, C.c_int]
+    lib.ref_gqa_attention.argtypes = [_p, _p, _p, _p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                      C.c_int, C.c_int, C.c_int]
     lib.ref_sample_token.restype = C.c_int
     lib.ref_sample_token.argtypes = [_p, C.c_int, _f, _f, C.c_int, _f, _p, C.c_int, C.c_long,
                                      C.POINTER(_f)]
@@ -181,6 +187,27 @@ class Oracle:
                                 hs, _ptr(np.ascontiguousarray(uniforms, np.float32)), temperature,
                                 rep, ctx, freq, _ptr(out))
         return out
+
+    def decode_attention(self, q, k_cache, v_cache, start, length):
+        """q [B, H, hd]; caches [B, cap, Hk, hd]; start, length int32 [B]."""
+        dt = dtype_code(q)
+        q = np.ascontiguousarray(q)
+        k_cache = np.ascontiguousarray(k_cache, q.dtype)
+        v_cache = np.ascontiguousarray(v_cache, q.dtype)
+        B, H, hd = q.shape
+        _, cap, hk, _ = k_cache.shape
+        out = np.empty_like(q)
+        self.lib.or_decode_attention(dt, _ptr(out), H * hd, _ptr(q), H * hd, hd, _ptr(k_cache),
+                                     _ptr(v_cache), cap * hk * hd,
+                                     _ptr(np.ascontiguousarray(start, np.int32)),
+                                     _ptr(np.ascontiguousarray(length, np.int32)), cap, B, H, hk,
+                                     hd)
+        return out
+
+    def kv_ring_advance(self, start, length, capacity):
+        s, n = C.c_int32(start), C.c_int32(length)
+        slot = self.lib.or_kv_ring_advance(C.byref(s), C.byref(n), capacity)
+        return slot, s.value, n.value
 
 
 def dtype_code(a: np.ndarray) -> int:

@@ -1,0 +1,141 @@
+"""GPU decode attention over a ring KV cache (core/cpu_ops.cpp:173-240)
+through the C ABI.
+
+The kernel and the oracle take every sum in the same fixed order, so they
+must agree bit for bit in all three element types.  Against the reference
+itself (its gqa_attention compiled with the shim, sequential sums) the fp32
+output must be within 1e-6 x max|v| -- the two summation orders each stay
+within about 1e-7 x max|v| of the exact (fp64) result."""
+import zlib
+
+import numpy as np
+import pytest
+
+from test_gpu_layer_ops import rand, to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+REF_TOL = 1e-6  # x max|v|, fp32 vs the reference's sequential sums
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def make_case(rng, B, H, hk, hd, cap, starts, lens, dt):
+    q = rand(rng, (B, H, hd), dt)
+    k = rand(rng, (B, cap, hk, hd), dt)
+    v = rand(rng, (B, cap, hk, hd), dt)
+    return q, k, v, np.array(starts, np.int32), np.array(lens, np.int32)
+
+
+def run_gpu(ane, q, k, v, st, ln, dt, max_len=None, workspace=None):
+    torch = _torch()
+    out = ane.decode_attention(to_dev(q, dt), to_dev(k, dt), to_dev(v, dt),
+                               torch.from_numpy(st).cuda(), torch.from_numpy(ln).cuda(),
+                               max_len=max_len, workspace=workspace)
+    torch.cuda.synchronize()
+    return to_host(out, dt)
+
+
+def bits(a):
+    return a.view(np.uint32) if a.dtype == np.float32 else a.view(np.uint16)
+
+
+SHAPES = [
+    # B, H, Hk, hd, cap, starts, lens
+    (1, 16, 8, 128, 4096, [0], [4096]),      # Qwen3-0.6B, full ring
+    (1, 16, 8, 128, 4096, [1000], [4096]),   # full ring, wrapped
+    (1, 16, 8, 128, 4096, [4000], [200]),    # wraps inside the window
+    (1, 16, 8, 128, 512, [3], [1]),          # one key
+    (1, 16, 8, 128, 512, [0], [64]),         # exactly one split
+    (1, 16, 8, 128, 512, [0], [65]),         # one key into the second split
+    (1, 32, 8, 128, 300, [250], [290]),      # Qwen3-8B grouping, odd capacity
+    (1, 40, 8, 128, 256, [17], [255]),       # 5 q heads per kv head
+    (1, 8, 8, 64, 100, [99], [37]),          # head_dim 64, no grouping
+    (1, 24, 8, 64, 1000, [5], [999]),        # 3 q heads per kv head
+    (1, 16, 2, 256, 129, [5], [129]),        # head_dim 256, 8 per kv head
+    (3, 16, 8, 128, 700, [0, 650, 13], [700, 0, 333]),  # batch, an empty sequence
+]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: f"B{s[0]}H{s[1]}k{s[2]}d{s[3]}c{s[4]}")
+def test_attention_matches_oracle(ane, oracle, dt, shape):
+    B, H, hk, hd, cap, starts, lens = shape
+    rng = np.random.default_rng(zlib.crc32(repr((B, H, hk, hd, cap, dt)).encode()))
+    q, k, v, st, ln = make_case(rng, B, H, hk, hd, cap, starts, lens, dt)
+    want = oracle.decode_attention(q, k, v, st, ln)
+    got = run_gpu(ane, q, k, v, st, ln, dt)
+    assert np.array_equal(bits(got), bits(want)), (
+        f"{int((bits(got) != bits(want)).sum())} of {got.size} differ")
+
+
+@pytest.mark.parametrize("shape", SHAPES[:9], ids=lambda s: f"H{s[1]}k{s[2]}d{s[3]}c{s[4]}l{s[6][0]}")
+def test_attention_matches_reference(ane, ref, shape):
+    B, H, hk, hd, cap, starts, lens = shape
+    rng = np.random.default_rng(7)
+    q, k, v, st, ln = make_case(rng, B, H, hk, hd, cap, starts, lens, "f32")
+    got = run_gpu(ane, q, k, v, st, ln, "f32")
+    want = np.empty_like(q[0])
+    from oracle_lib import _ptr
+    ref.ref_gqa_attention(_ptr(want), _ptr(q[0]), _ptr(np.ascontiguousarray(k[0])),
+                          _ptr(np.ascontiguousarray(v[0])), H, hk, hd, hd, int(st[0]), int(ln[0]),
+                          cap)
+    tol = REF_TOL * np.abs(v).max()
+    assert np.abs(got[0] - want).max() <= tol
+
+
+def test_attention_caller_workspace_two_calls(ane, oracle):
+    """A caller-provided zero-filled workspace gives the same bits as the
+    library-held one, twice in a row (the split counters are left at zero)."""
+    torch = _torch()
+    rng = np.random.default_rng(11)
+    B, H, hk, hd, cap = 2, 16, 8, 128, 1024
+    q, k, v, st, ln = make_case(rng, B, H, hk, hd, cap, [100, 0], [1024, 517], "f32")
+    want = oracle.decode_attention(q, k, v, st, ln)
+    nbytes = ane.decode_attention_workspace_size(B, H, hk, hd, cap)
+    assert nbytes > 0
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    for _ in range(2):
+        got = run_gpu(ane, q, k, v, st, ln, "f32", workspace=ws)
+        assert np.array_equal(bits(got), bits(want))
+    assert int(ws[: B * hk * 4].count_nonzero()) == 0
+    got = run_gpu(ane, q, k, v, st, ln, "f32")
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_attention_max_len_sizes_launch(ane, oracle):
+    """max_len below the capacity launches fewer splits; same bits."""
+    rng = np.random.default_rng(12)
+    q, k, v, st, ln = make_case(rng, 1, 16, 8, 128, 4096, [4090], [300], "f16")
+    want = oracle.decode_attention(q, k, v, st, ln)
+    got = run_gpu(ane, q, k, v, st, ln, "f16", max_len=300)
+    assert np.array_equal(bits(got), bits(want))
+
+
+def test_attention_bad_cache_flag(ane):
+    """len > max_len or > capacity, or start outside: zeros and a flag."""
+    rng = np.random.default_rng(13)
+    ane.read_status_flags(clear=True)
+    q, k, v, st, ln = make_case(rng, 3, 16, 8, 128, 256, [0, 300, 0], [100, 10, 257], "f32")
+    got = run_gpu(ane, q, k, v, st, ln, "f32", max_len=256)
+    flags = ane.read_status_flags(clear=True)
+    assert flags & ane.FLAG_BAD_CACHE
+    assert not np.any(got[1]) and not np.any(got[2])
+    assert np.any(got[0])
+
+
+def test_attention_rejects_unsupported(ane):
+    torch = _torch()
+    q = torch.zeros((1, 16, 96), device="cuda")
+    k = torch.zeros((1, 64, 8, 96), device="cuda")
+    st = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(ane.AneCudaError) as e:
+        ane.decode_attention(q, k, k, st, st)
+    assert e.value.status == ane.ERR_UNSUPPORTED
+    q = torch.zeros((1, 32, 128), device="cuda")
+    k = torch.zeros((1, 64, 2, 128), device="cuda")  # 16 q heads per kv head
+    with pytest.raises(ane.AneCudaError):
+        ane.decode_attention(q, k, k, st, st)

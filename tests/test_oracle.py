@@ -197,3 +197,49 @@ def test_layer_chain_f16_vs_reference(oracle, ref):
     assert f16_ulp_diff(yo, yr).max() <= 2
     assert f16_ulp_diff(qo, qr).max() <= 2
     assert f16_ulp_diff(ho, hr).max() <= 2
+
+
+# ---------------------------------------------------------- decode attention
+@pytest.mark.parametrize("H,hk,hd,cap,start,ln", [
+    (16, 8, 128, 4096, 1000, 4096), (32, 8, 128, 300, 250, 290), (16, 8, 128, 512, 7, 1),
+    (8, 8, 64, 100, 99, 37), (16, 2, 256, 129, 5, 129), (16, 8, 128, 64, 0, 0)])
+def test_attention_oracle_vs_reference(oracle, ref, H, hk, hd, cap, start, ln):
+    """The pinned split order stays within 1e-6 x max|v| of the reference's
+    sequential sums (core/cpu_ops.cpp:173-240 with the shim)."""
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((1, H, hd)).astype(np.float32)
+    k = rng.standard_normal((1, cap, hk, hd)).astype(np.float32)
+    v = rng.standard_normal((1, cap, hk, hd)).astype(np.float32)
+    got = oracle.decode_attention(q, k, v, [start], [ln])[0]
+    want = np.empty((H, hd), np.float32)
+    ref.ref_gqa_attention(ptr(want), ptr(q), ptr(k), ptr(v), H, hk, hd, hd, start, ln, cap)
+    assert np.abs(got - want).max() <= 1e-6 * np.abs(v).max()
+    if ln == 0:
+        assert not np.any(got) and not np.any(want)
+
+
+def test_attention_oracle_half_types(oracle):
+    """fp16 caches: the fp32 arithmetic on the widened values, rounded once
+    at the end.  (head_dim 256: 8 elements per lane for both element sizes,
+    so fp16 and fp32 take the same summation order.)"""
+    rng = np.random.default_rng(4)
+    q = rng.standard_normal((1, 16, 256)).astype(np.float16)
+    k = rng.standard_normal((1, 200, 8, 256)).astype(np.float16)
+    v = rng.standard_normal((1, 200, 8, 256)).astype(np.float16)
+    o16 = oracle.decode_attention(q, k, v, [150], [200])
+    o32 = oracle.decode_attention(q.astype(np.float32), k.astype(np.float32),
+                                  v.astype(np.float32), [150], [200])
+    assert np.array_equal(o16, o32.astype(np.float16))
+
+
+def test_kv_ring_advance():
+    """models/llm/qwen3.cpp:475-484: fill, then overwrite the oldest slot."""
+    from oracle_lib import Oracle
+    o = Oracle()
+    start, ln, cap = 0, 0, 4
+    slots = []
+    for _ in range(7):
+        slot, start, ln = o.kv_ring_advance(start, ln, cap)
+        slots.append(slot)
+    assert slots == [0, 1, 2, 3, 0, 1, 2]
+    assert (start, ln) == (3, 4)
