@@ -47,6 +47,9 @@ _SIGS = {
     "ane_cuda_write_ane_blobs": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
     "ane_cuda_convert_model": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
     "ane_cuda_decode_attention_workspace_size": (_i64, [_i64, _i, _i, _i, _i]),
+    "ane_cuda_decode_attention_static_capacity": (_i64, []),
+    "ane_cuda_decode_attention_static": (_i, [_i, _p, _i64, _p, _i64, _i, _p, _p, _i64, _p, _p,
+                                              _i, _i64, _i, _i, _i, _i, _p]),
     "ane_cuda_decode_attention": (_i, [_i, _p, _i64, _p, _i64, _i, _p, _p, _i64, _p, _p, _i,
                                        _i64, _i, _i, _i, _i, _p, _i64, _p]),
 }
@@ -253,4 +256,22 @@ def decode_attention(q, k_cache, v_cache, cache_start, cache_len, max_len=None, 
         _dt(q), _ptr(out), out.stride(0), _ptr(q), q.stride(0), q.stride(1), _ptr(k_cache),
         _ptr(v_cache), k_cache.stride(0), _ptr(cache_start), _ptr(cache_len), capacity, batch,
         n_heads, n_kv, head_dim, max_len, _ptr(workspace), ws_bytes, _stream(q)))
+    return out
+
+
+def decode_attention_static(q, k_cache, v_cache, cache_start, cache_len, max_len=None, out=None):
+    """decode_attention with the split scratch in a fixed device array: allocates
+    nothing; calls must not overlap in time (order them on one stream)."""
+    torch = _torch()
+    _cuda(q, k_cache, v_cache, cache_start, cache_len)
+    batch, n_heads, head_dim = q.shape
+    _, capacity, n_kv, _ = k_cache.shape
+    if max_len is None:
+        max_len = capacity
+    if out is None:
+        out = torch.empty_like(q)
+    _check("decode_attention_static", lib().ane_cuda_decode_attention_static(
+        _dt(q), _ptr(out), out.stride(0), _ptr(q), q.stride(0), q.stride(1), _ptr(k_cache),
+        _ptr(v_cache), k_cache.stride(0), _ptr(cache_start), _ptr(cache_len), capacity, batch,
+        n_heads, n_kv, head_dim, max_len, _stream(q)))
     return out

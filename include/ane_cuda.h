@@ -198,6 +198,28 @@ ANE_CUDA_API int ane_cuda_decode_attention(int dtype, void* out, int64_t out_str
                                            int head_dim, int max_len, void* workspace,
                                            int64_t workspace_bytes, void* stream);
 
+/* ---- decode attention without allocation ----------------------------------
+ * No counterpart in the reference (its gqa_attention mallocs a score buffer
+ * per call, core/cpu_ops.cpp:191).  The same computation and results as
+ * ane_cuda_decode_attention, with the split scratch taken from a fixed
+ * array in the library's device image (ane_cuda_decode_attention_static_capacity()
+ * bytes per device) instead of a workspace: the call allocates no memory.
+ * For callers whose device-memory footprint must not change once running,
+ * or that cannot take cudaMalloc's synchronisation in a decode loop.
+ * Problems needing more scratch than the capacity are rejected
+ * (ANE_CUDA_ERR_INVALID_ARG).  The array is shared by all calls on a
+ * device: calls whose executions overlap race on it -- order them on one
+ * stream. */
+ANE_CUDA_API int64_t ane_cuda_decode_attention_static_capacity(void);
+ANE_CUDA_API int ane_cuda_decode_attention_static(int dtype, void* out, int64_t out_stride,
+                                                  const void* q, int64_t q_stride,
+                                                  int q_head_stride, const void* k_cache,
+                                                  const void* v_cache, int64_t cache_stride,
+                                                  const int32_t* cache_start,
+                                                  const int32_t* cache_len, int cache_capacity,
+                                                  int64_t batch, int n_heads, int n_kv_heads,
+                                                  int head_dim, int max_len, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
