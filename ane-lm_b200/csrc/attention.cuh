@@ -69,6 +69,13 @@ struct AttnShape {
     static constexpr int GL = HD / EPL;                    // lanes per key
     static constexpr int KPW = kWarp / GL;                 // keys per warp step
     static constexpr int U = kAttnWarps * KPW;             // key groups per CTA
+    static constexpr int NKEY = kAttnKeys / U;             // keys per group in P.V
+    // fp32 V rows go straight to registers (prefetched at the start) when a
+    // lane's share is at most 16 vectors: that halves the shared memory of
+    // a CTA, so a batch-1 launch fits in one wave.  16-bit rows are staged
+    // in shared memory like K: their kernels are issue-bound at large
+    // batch, and the extra registers would cost occupancy.
+    static constexpr bool VREG = sizeof(typename T::storage) == 4 && NKEY * NV <= 16;
     static_assert(EPL % V == 0 && GL * EPL == HD && KPW * GL == kWarp, "head_dim layout");
 };
 
@@ -76,11 +83,16 @@ struct AttnShape {
 template <int G>
 __host__ __device__ constexpr int attn_prow() { return G <= 1 ? 1 : G <= 2 ? 2 : G <= 4 ? 4 : 8; }
 
+template <typename T, int HD>
+__host__ __device__ constexpr size_t attn_rows_bytes() {  // K rows, and V rows unless they live in registers
+    return (AttnShape<T, HD>::VREG ? 1 : 2) * (size_t)kAttnKeys * HD * sizeof(typename T::storage);
+}
+
 template <typename T, int HD, int G>
-constexpr size_t attn_smem_bytes() {
-    return 2 * (size_t)kAttnKeys * HD * sizeof(typename T::storage)  // K, V rows
-           + (size_t)kAttnKeys * attn_prow<G>() * sizeof(float)      // P, key-major
-           + (size_t)kAttnWarps * G * HD * sizeof(float);            // warp partials
+__host__ __device__ constexpr size_t attn_smem_bytes() {
+    return attn_rows_bytes<T, HD>()
+           + (size_t)kAttnKeys * attn_prow<G>() * sizeof(float)  // P, key-major
+           + (size_t)kAttnWarps * G * HD * sizeof(float);        // warp partials
 }
 
 // Dots of one 32-key block (keys kb*32 ..) with GC q heads held in registers.
@@ -145,13 +157,15 @@ decode_attention_kernel(const AttnArgs a) {
     using S = typename T::storage;
     using Sh = AttnShape<T, HD>;
     constexpr int V = Sh::V, EPL = Sh::EPL, NV = Sh::NV, GL = Sh::GL, KPW = Sh::KPW, U = Sh::U;
+    constexpr int NKEY = Sh::NKEY;
+    constexpr bool VREG = Sh::VREG;
     constexpr int PROW = attn_prow<G>();
     constexpr int GA = (G + 1) / 2;  // heads of warps 0-1; warps 2-3 take the other G - GA
     constexpr uint32_t ROW = HD * sizeof(S);
     extern __shared__ __align__(16) unsigned char smem[];
     S* const sK = reinterpret_cast<S*>(smem);
-    S* const sV = sK + kAttnKeys * HD;
-    float* const s_p = reinterpret_cast<float*>(sV + kAttnKeys * HD);  // [key][PROW]
+    S* const sV = sK + kAttnKeys * HD;  // only when !VREG
+    float* const s_p = reinterpret_cast<float*>(smem + attn_rows_bytes<T, HD>());  // [key][PROW]
     float* const s_red = s_p + kAttnKeys * PROW;                      // [warp][G][HD]
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
@@ -187,19 +201,37 @@ decode_attention_kernel(const AttnArgs a) {
     __syncthreads();
     if (tid == 0) {
         mbar_expect_tx(&bars[0], (uint32_t)n * ROW);
-        mbar_expect_tx(&bars[1], (uint32_t)n * ROW);
+        if constexpr (!VREG) mbar_expect_tx(&bars[1], (uint32_t)n * ROW);
     }
     __syncthreads();  // byte counts registered before any copy is issued
+    // ring position of local key i (models/llm/qwen3.cpp:190-204)
+    auto row_off = [&](int i) {
+        int slot = start + t0 + i;
+        if (slot >= a.capacity) slot -= a.capacity;
+        return b * a.cache_stride + ((int64_t)slot * a.n_kv + kvh) * HD;
+    };
     {
         const int i = tid & (kAttnKeys - 1);  // threads 0-63 copy K rows, 64-127 V rows
         if (i < n) {
-            int slot = start + t0 + i;  // ring position (models/llm/qwen3.cpp:190-204)
-            if (slot >= a.capacity) slot -= a.capacity;
-            const int64_t off = b * a.cache_stride + ((int64_t)slot * a.n_kv + kvh) * HD;
             if (tid < kAttnKeys)
-                bulk_load(sK + i * HD, static_cast<const S*>(a.k_cache) + off, ROW, &bars[0]);
-            else
-                bulk_load(sV + i * HD, static_cast<const S*>(a.v_cache) + off, ROW, &bars[1]);
+                bulk_load(sK + i * HD, static_cast<const S*>(a.k_cache) + row_off(i), ROW, &bars[0]);
+            else if constexpr (!VREG)
+                bulk_load(sV + i * HD, static_cast<const S*>(a.v_cache) + row_off(i), ROW, &bars[1]);
+        }
+    }
+    // P.V layout: key group u (lanes j*GL .. of warp w) takes keys u, u+U, ...
+    const int j = lane / GL, l = lane % GL;
+    const int u = w * KPW + j;
+    uint4 vreg[VREG ? NKEY : 1][NV];
+    if constexpr (VREG) {  // this lane's V chunks of its P.V keys, in flight during the scores
+#pragma unroll
+        for (int r = 0; r < NKEY; r++) {
+            const int k = u + r * U;
+            if (k < n) {
+                const S* vp = static_cast<const S*>(a.v_cache) + row_off(k) + l * EPL;
+#pragma unroll
+                for (int c = 0; c < NV; c++) vreg[r][c] = ld_stream(vp + c * V);
+            }
         }
     }
 
@@ -249,24 +281,29 @@ decode_attention_kernel(const AttnArgs a) {
             s_p[i * PROW + g0 + g] = e;
         }
     }
-    if (!__syncthreads_and(mbar_wait_bounded(&bars[1], 0))) {
+    if constexpr (VREG) {
+        __syncthreads();
+    } else if (!__syncthreads_and(mbar_wait_bounded(&bars[1], 0))) {
         if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
         return;
     }
 
     // ---- 2b. un-normalised P.V: key group u takes keys u, u+U, ... -------
-    const int j = lane / GL, l = lane % GL;
-    const int u = w * KPW + j;
     float acc[G][EPL];
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < EPL; e++) acc[g][e] = 0.0f;
-    for (int k = u; k < n; k += U) {
+#pragma unroll
+    for (int r = 0; r < NKEY; r++) {
+        const int k = u + r * U;
+        if (k >= n) break;  // keys of a group ascend
         float vf[EPL];
 #pragma unroll
-        for (int c = 0; c < NV; c++)
-            unpack<T>(*reinterpret_cast<const uint4*>(sV + k * HD + l * EPL + c * V), &vf[c * V]);
+        for (int c = 0; c < NV; c++) {
+            if constexpr (VREG) unpack<T>(vreg[r][c], &vf[c * V]);
+            else unpack<T>(*reinterpret_cast<const uint4*>(sV + k * HD + l * EPL + c * V), &vf[c * V]);
+        }
         float p[PROW];
         if constexpr (PROW >= 4) {
 #pragma unroll
@@ -347,21 +384,38 @@ decode_attention_kernel(const AttnArgs a) {
     if (tid == 0) a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
 
     // ---- 3. merge the splits (last CTA of this kv head and sequence) -------
+    // (m_j, l_j) of up to FT splits at a time in shared memory over the K
+    // rows (no longer needed); M = max m_j; f_j = exp(m_j - M) replaces m_j;
+    // O and L as four fmaf chains over j = c4 (mod 4), in order of j.
+    constexpr int FT = (int)((attn_rows_bytes<T, HD>() / sizeof(float2)) / G) & ~3;
+    constexpr int COLS = HD / 4;
+    constexpr int ITEMS = G * 4 * COLS;  // (g, chain, float4 column)
+    constexpr int IPT = (ITEMS + kAttnThreads - 1) / kAttnThreads;
+    float2* const s_ml = reinterpret_cast<float2*>(smem);  // [G][FT]
+    auto load_ml = [&](int s0, int ns) {
+        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
+            const int g = idx / ns, s = s0 + idx % ns;
+            const float2* ml = reinterpret_cast<const float2*>(a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2);
+            s_ml[g * FT + (s - s0)] = __ldcg(ml + s);
+        }
+    };
+    const bool one_tile = nsplit <= FT;
+    if (one_tile) {
+        load_ml(0, nsplit);
+        __syncthreads();
+    }
     for (int g = w; g < G; g += kAttnWarps) {
-        const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
         float mx = -INFINITY;
-        for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, __ldcg(ml + 2 * s));
+        if (one_tile) {
+            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, s_ml[g * FT + s].x);
+        } else {
+            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
+            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, __ldcg(ml + 2 * s));
+        }
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         if (lane == 0) s_M[g] = mx;
     }
-    // f_j = exp(m_j - M) in tiles of FT splits over the K / V rows (no longer
-    // needed); O and L as four chains over j = c4 (mod 4), in order of j.
-    constexpr int FT = (int)((2 * (size_t)kAttnKeys * HD * sizeof(S) / sizeof(float)) / G) & ~3;
-    constexpr int COLS = HD / 4;
-    constexpr int ITEMS = G * 4 * COLS;  // (g, chain, float4 column)
-    constexpr int IPT = (ITEMS + kAttnThreads - 1) / kAttnThreads;
-    float* const s_f = reinterpret_cast<float*>(smem);  // [G][FT]
     float4 o[IPT];
 #pragma unroll
     for (int it = 0; it < IPT; it++) o[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -369,10 +423,13 @@ decode_attention_kernel(const AttnArgs a) {
     for (int s0 = 0; s0 < nsplit; s0 += FT) {
         const int s1 = min(nsplit, s0 + FT), ns = s1 - s0;
         __syncthreads();  // s_M ready / the previous tile consumed
+        if (!one_tile) {
+            load_ml(s0, ns);
+            __syncthreads();
+        }
         for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
-            const int g = idx / ns, s = s0 + idx % ns;
-            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
-            s_f[g * FT + (s - s0)] = pinned_expf(__fsub_rn(__ldcg(ml + 2 * s), s_M[g]));
+            float2& e = s_ml[(idx / ns) * FT + idx % ns];
+            e.x = pinned_expf(__fsub_rn(e.x, s_M[idx / ns]));
         }
         __syncthreads();
 #pragma unroll
@@ -382,11 +439,11 @@ decode_attention_kernel(const AttnArgs a) {
                 const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
                 const float4* po =
                     reinterpret_cast<const float4*>(a.part_o + (pbase + (int64_t)g * a.max_splits) * HD) + col;
-                const float* f = s_f + g * FT;
-#pragma unroll 8
+                const float2* f = s_ml + g * FT - s0;
+#pragma unroll 16
                 for (int s = s0 + c4; s < s1; s += 4) {
                     const float4 v = __ldcg(po + (int64_t)s * COLS);
-                    const float fs = f[s - s0];
+                    const float fs = f[s].x;
                     o[it].x = __fmaf_rn(v.x, fs, o[it].x);
                     o[it].y = __fmaf_rn(v.y, fs, o[it].y);
                     o[it].z = __fmaf_rn(v.z, fs, o[it].z);
@@ -396,10 +453,8 @@ decode_attention_kernel(const AttnArgs a) {
         }
         if (tid < 4 * G) {
             const int c4 = tid & 3, g = tid >> 2;
-            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
-            const float* f = s_f + g * FT;
-#pragma unroll 8
-            for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(__ldcg(ml + 2 * s + 1), f[s - s0], Lc);
+            const float2* f = s_ml + g * FT - s0;
+            for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(f[s].y, f[s].x, Lc);
         }
     }
 #pragma unroll
