@@ -310,8 +310,8 @@ def time_e2e_chain(torch, ane, rows, steps, chunks=8):
 
 def time_extras(torch, ane, reps=20):
     """Secondary configs (per GPU): BF16->FP16 convert of a Qwen3-8B-shaped
-    checkpoint (flat), the 256-row sampler, the Qwen3-1.7B prefill chain and
-    the Qwen3-0.6B batch-1 decode chain latency."""
+    checkpoint (flat), the 256-row sampler, the Qwen3-1.7B prefill chain,
+    the Qwen3-0.6B batch-1 decode chain latency and decode attention."""
     import ctypes as C
     L = ane.lib()
     out = {}
@@ -395,7 +395,59 @@ def time_extras(torch, ane, reps=20):
     ms = timed(graph.replay, 200)
     out["decode_qwen3_0p6b_b1"] = {"us_per_token": round(ms * 1e3, 2), "kernels": 4}
     del graph
+
+    # decode attention over the KV ring: Qwen3-0.6B batch 1 with the
+    # reference's fp32 cache, and Qwen3-8B batch 64 with an fp16 cache; 4096
+    # keys, ring start mid-cache (wrapped).  CUDA graph of back-to-back calls
+    # over rotating cache copies (more than L2 in total).
+    peak, _ = measured_peak()
+    for name, (B, H, hk, dt) in {"attention_qwen3_0p6b_b1_l4096_f32": (1, 16, 8, torch.float32),
+                                 "attention_qwen3_8b_b64_l4096_f16": (64, 32, 8, torch.float16)}.items():
+        us, gbs = time_attention(torch, ane, B, H, hk, 128, 4096, dt)
+        out[name] = {"us": round(us, 2), "gb_s": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
     return out
+
+
+def time_attention(torch, ane, B, H, hk, hd, ln, dt, start=1000):
+    """(us per call, GB/s of K and V read) for ane.decode_attention."""
+    es = torch.tensor([], dtype=dt).element_size()
+    kv_bytes = 2 * B * ln * hk * hd * es
+    ncopy = max(1, min(16, (512 << 20) // kv_bytes + 1))
+    g = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn(B, H, hd, device="cuda", generator=g).to(dt)
+    ks = [torch.randn(B, ln, hk, hd, device="cuda", generator=g).to(dt) for _ in range(ncopy)]
+    vs = [torch.randn(B, ln, hk, hd, device="cuda", generator=g).to(dt) for _ in range(ncopy)]
+    st = torch.full((B,), start, dtype=torch.int32, device="cuda")
+    ln_t = torch.full((B,), ln, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(max(1, ane.decode_attention_workspace_size(B, H, hk, hd, ln)),
+                     dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(q)
+    s = torch.cuda.Stream()
+    reps = ncopy * max(1, 32 // ncopy)
+    with torch.cuda.stream(s):
+        for i in range(3):
+            ane.decode_attention(q, ks[i % ncopy], vs[i % ncopy], st, ln_t, max_len=ln, out=out,
+                                 workspace=ws)
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(reps):
+                ane.decode_attention(q, ks[i % ncopy], vs[i % ncopy], st, ln_t, max_len=ln,
+                                     out=out, workspace=ws)
+        graph.replay()
+        s.synchronize()
+        ts = []
+        for _ in range(10):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            graph.replay()
+            b.record(s)
+            b.synchronize()
+            ts.append(a.elapsed_time(b) / reps)
+    ts.sort()
+    ms = ts[len(ts) // 2]
+    del graph
+    return ms * 1e3, kv_bytes / ms / 1e6
 
 
 # ---------------------------------------------------------------------------
@@ -636,6 +688,18 @@ def run_ncu_case(cases, rows=16384):
             assert L.ane_cuda_sample_rows(P(logits), r, v, v, P(hist), P(hlen), 1024, P(u), 0.6,
                                           1.2, 256, 0.1, P(tok), sp) == 0
         torch.cuda.synchronize()
+    if "attention" in cases:
+        for B, H, hk, ln, dt in ((16, 32, 8, 4096, torch.float16), (1, 16, 8, 4096, torch.float32)):
+            g = torch.Generator(device="cuda").manual_seed(9)
+            q = torch.randn(B, H, 128, device="cuda", generator=g).to(dt)
+            k = torch.randn(B, ln, hk, 128, device="cuda", generator=g).to(dt)
+            v = torch.randn(B, ln, hk, 128, device="cuda", generator=g).to(dt)
+            st = torch.full((B,), 1000, dtype=torch.int32, device="cuda")
+            n = torch.full((B,), ln, dtype=torch.int32, device="cuda")
+            for _ in range(2):
+                ane.decode_attention(q, k, v, st, n, max_len=ln)
+            torch.cuda.synchronize()
+            del q, k, v
     print("ncu case done:", ",".join(sorted(cases)), flush=True)
 
 
@@ -648,7 +712,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--ncu-case", default="",
-                    help="comma list of chain,convert,sampler: run the small profiling case and exit")
+                    help="comma list of chain,convert,sampler,attention: run the small profiling "
+                         "case and exit")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case(set(args.ncu_case.split(",")))
