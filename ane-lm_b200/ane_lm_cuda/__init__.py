@@ -20,6 +20,7 @@ HEADER = os.path.join(REPO, "include", "ane_cuda.h")
 OK, ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 F32, F16, BF16 = 0, 1, 2
 FLAG_BAD_TOKEN_ID = 0x1
+ROUND_NEAREST, ROUND_TRUNCATE = 0, 1
 FLAG_BAD_CACHE = 0x2
 FLAG_WAIT_TIMEOUT = 0x4
 
@@ -46,6 +47,8 @@ _SIGS = {
     "ane_cuda_sample_rows": (_i, [_p, _i64, _i, _i64, _p, _p, _i64, _p, _f, _f, _i, _f, _p, _p]),
     "ane_cuda_write_ane_blobs": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
     "ane_cuda_convert_model": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
+    "ane_cuda_ane_pack": (_i, [_i, _p, _p, _i64, _i64, _i, _i, _p]),
+    "ane_cuda_ane_unpack": (_i, [_p, _i64, _p, _i64, _i, _i, _p]),
     "ane_cuda_decode_attention_workspace_size": (_i64, [_i64, _i, _i, _i, _i]),
     "ane_cuda_decode_attention_static_capacity": (_i64, []),
     "ane_cuda_decode_attention_static": (_i, [_i, _p, _i64, _p, _i64, _i, _p, _p, _i64, _p, _p,
@@ -274,4 +277,30 @@ def decode_attention_static(q, k_cache, v_cache, cache_start, cache_len, max_len
         _dt(q), _ptr(out), out.stride(0), _ptr(q), q.stride(0), q.stride(1), _ptr(k_cache),
         _ptr(v_cache), k_cache.stride(0), _ptr(cache_start), _ptr(cache_len), capacity, batch,
         n_heads, n_kv, head_dim, max_len, _stream(q)))
+    return out
+
+
+def ane_pack(x, round_mode=ROUND_NEAREST, spatial=32, surface=None):
+    """x [tokens, channels] float32 -> surfaces [ceil(tokens/spatial), channels, spatial]
+    int16 (fp16 bits).  Slots without a token keep `surface`'s contents (zeros)."""
+    torch = _torch()
+    _cuda(x, surface)
+    tokens, channels = x.shape
+    if surface is None:
+        surface = torch.zeros(((tokens + spatial - 1) // spatial, channels, spatial),
+                              dtype=torch.int16, device=x.device)
+    _check("ane_pack", lib().ane_cuda_ane_pack(round_mode, _ptr(surface), _ptr(x), x.stride(0),
+                                               tokens, channels, spatial, _stream(x)))
+    return surface
+
+
+def ane_unpack(surface, tokens, spatial=32, out=None):
+    """surfaces [n, channels, spatial] of fp16 bits -> out [tokens, channels] float32."""
+    torch = _torch()
+    _cuda(surface, out)
+    channels = surface.shape[1]
+    if out is None:
+        out = torch.empty((tokens, channels), dtype=torch.float32, device=surface.device)
+    _check("ane_unpack", lib().ane_cuda_ane_unpack(_ptr(out), out.stride(0), _ptr(surface), tokens,
+                                                   channels, spatial, _stream(surface)))
     return out

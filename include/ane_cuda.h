@@ -41,6 +41,12 @@ typedef enum {
 /* element types of activation rows and tables */
 typedef enum { ANE_CUDA_F32 = 0, ANE_CUDA_F16 = 1, ANE_CUDA_BF16 = 2 } ane_cuda_dtype;
 
+/* fp32 -> fp16 rounding at the ANE boundary */
+typedef enum {
+    ANE_CUDA_ROUND_NEAREST = 0,  /* native __fp16 store on arm64 (round to nearest even) */
+    ANE_CUDA_ROUND_TRUNCATE = 1  /* f32_to_f16 of include/ane_lm/common.h:58-71 (x86) */
+} ane_cuda_round;
+
 /* bits of the per-device status word */
 #define ANE_CUDA_FLAG_BAD_TOKEN_ID 0x1u /* a gather id was outside [0, vocab) */
 #define ANE_CUDA_FLAG_BAD_CACHE    0x2u /* a KV ring start / len outside the cache */
@@ -164,6 +170,24 @@ ANE_CUDA_API int ane_cuda_sample_rows(const float* logits, int64_t rows, int voc
                          int64_t history_stride, const float* uniforms, float temperature,
                          float repetition_penalty, int repetition_context,
                          float frequency_penalty, int32_t* out_tokens, void* stream);
+
+/* ---- fp32 <-> fp16 packing at the ANE boundary ---------------------------
+ * Replaces the element loops of ane_matvec (core/ane_runtime.cpp:611-653):
+ * input channel c of a token goes to element c * spatial of the fp16
+ * surface [channels][spatial] (ANE_SPATIAL = 32, core/ane_runtime.h:10), and
+ * output channel c is read back from element c * spatial.  Batched: token t
+ * of in[tokens][in_stride] uses surface t / spatial and spatial slot
+ * t % spatial of surface [ceil(tokens / spatial)][channels][spatial];
+ * elements of slots without a token are not written.  round_mode picks the
+ * arm64 conversion (round to nearest even; NaN -> quiet NaN 0x7E00 with the
+ * sign) or the x86 one (truncating f32_to_f16: Inf and NaN -> signed Inf).
+ * Unpacking widens exactly (NaN payloads kept).  Bit-exact.  spatial 32 with
+ * a 16-byte aligned surface takes the tiled path; other sizes are accepted. */
+ANE_CUDA_API int ane_cuda_ane_pack(int round_mode, uint16_t* surface, const float* in,
+                                   int64_t in_stride, int64_t tokens, int channels, int spatial,
+                                   void* stream);
+ANE_CUDA_API int ane_cuda_ane_unpack(float* out, int64_t out_stride, const uint16_t* surface,
+                                     int64_t tokens, int channels, int spatial, void* stream);
 
 /* ---- decode attention over a ring KV cache ----------------------------
  * Replaces gqa_attention (core/cpu_ops.cpp:173-240, declared at

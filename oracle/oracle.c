@@ -81,6 +81,24 @@ uint16_t or_f32_to_bf16_rne(float f) {
     return (uint16_t)(u >> 16);
 }
 
+/* The reference's truncating f32_to_f16 (include/ane_lm/common.h:58-71),
+ * used by the x86 branch of the ANE input packing (core/ane_runtime.cpp:
+ * 625-627): exponent re-bias by -112; >= 31 (Inf and NaN too) -> signed Inf;
+ * <= 0 -> the mantissa with its hidden bit shifted right, low bits dropped;
+ * below 2^-25 -> signed zero. */
+uint16_t or_f32_to_f16_trunc(float f) {
+    uint32_t u = f2u(f);
+    uint16_t sign = (uint16_t)((u >> 16) & 0x8000u);
+    int32_t e = (int32_t)((u >> 23) & 0xFFu) - 112;
+    uint32_t frac = u & 0x7FFFFFu;
+    if (e <= 0) {
+        if (e < -10) return sign;
+        return (uint16_t)(sign | (uint16_t)(((frac | 0x800000u) >> (1 - e)) >> 13));
+    }
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    return (uint16_t)(sign | (uint16_t)(e << 10) | (uint16_t)(frac >> 13));
+}
+
 /* include/ane_lm/common.h:35-56 (exact widening) */
 float or_f16_to_f32(uint16_t h) {
     uint32_t sign = (uint32_t)(h >> 15) << 31;
@@ -513,6 +531,37 @@ void or_decode_attention(int dt, void* out, int64_t out_stride,
     free(vbuf);
     free(acc);
     free(O);
+}
+
+/* ------------------------------------------------------------------ */
+/* fp32 <-> fp16 packing at the ANE boundary, core/ane_runtime.cpp:611-653 */
+/* ------------------------------------------------------------------ */
+
+/* ane_matvec writes channel c of its one token to element c * ANE_SPATIAL of
+ * the fp16 input surface [channels][32] (:622-629) and reads channel c of the
+ * output from element c * ANE_SPATIAL (:643-650).  Batched: token t of
+ * `tokens` goes to surface t / spatial, spatial slot t % spatial; elements of
+ * other slots are left as they are.  round_mode 0 = round to nearest even
+ * (the native __fp16 store on arm64, :604-609), NaN -> quiet NaN 0x7E00
+ * with the sign; 1 = the truncating f32_to_f16 of the x86 branch. */
+void or_ane_pack(int round_mode, uint16_t* surface, const float* in, int64_t in_stride,
+                 int64_t tokens, int channels, int spatial) {
+    for (int64_t t = 0; t < tokens; t++) {
+        uint16_t* sf = surface + (t / spatial) * (int64_t)channels * spatial + t % spatial;
+        for (int c = 0; c < channels; c++) {
+            const float x = in[t * in_stride + c];
+            sf[(int64_t)c * spatial] = round_mode ? or_f32_to_f16_trunc(x) : or_f32_to_f16_rne(x);
+        }
+    }
+}
+
+/* The output side: out[t][c] = (float) surface element (exact). */
+void or_ane_unpack(float* out, int64_t out_stride, const uint16_t* surface, int64_t tokens,
+                   int channels, int spatial) {
+    for (int64_t t = 0; t < tokens; t++) {
+        const uint16_t* sf = surface + (t / spatial) * (int64_t)channels * spatial + t % spatial;
+        for (int c = 0; c < channels; c++) out[t * out_stride + c] = or_f16_to_f32(sf[(int64_t)c * spatial]);
+    }
 }
 
 /* models/llm/qwen3.cpp:475-484: append while the ring has room, else

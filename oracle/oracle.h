@@ -49,6 +49,7 @@ enum { OR_F32 = 0, OR_F16 = 1, OR_BF16 = 2 };
 uint16_t or_bf16_to_f16(uint16_t bf);
 void     or_bf16_to_f16_vec(uint16_t* out, const uint16_t* in, int64_t n);
 uint16_t or_f32_to_f16_rne(float f);
+uint16_t or_f32_to_f16_trunc(float f);
 uint16_t or_f32_to_bf16_rne(float f);
 float    or_f16_to_f32(uint16_t h);
 float    or_bf16_to_f32(uint16_t h);
@@ -84,6 +85,12 @@ int64_t or_embedding_gather(void* out, int out_dtype, const void* table,
                             int64_t rows, int vocab, int hidden);
 
 void or_softmax_rows(float* x, int64_t rows, int n, int64_t stride);
+
+/* ---- fp32 <-> fp16 at the ANE boundary (core/ane_runtime.cpp:611-653) ---- */
+void or_ane_pack(int round_mode, uint16_t* surface, const float* in, int64_t in_stride,
+                 int64_t tokens, int channels, int spatial);
+void or_ane_unpack(float* out, int64_t out_stride, const uint16_t* surface, int64_t tokens,
+                   int channels, int spatial);
 
 /* ---- decode attention (core/cpu_ops.cpp:173-240) ---- */
 void or_decode_attention(int dtype, void* out, int64_t out_stride,

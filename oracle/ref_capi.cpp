@@ -31,6 +31,15 @@ void ref_bf16_to_f16_vec(uint16_t* out, const uint16_t* in, int64_t n) {
 uint16_t ref_f32_to_f16(float f) { return ane_lm::f32_to_f16(f); }
 float ref_f16_to_f32(uint16_t h) { return ane_lm::f16_to_f32(h); }
 
+/* The element conversions of ane_matvec's x86 branch
+ * (core/ane_runtime.cpp:625-627 and :646-648), over arrays. */
+void ref_f32_to_f16_vec(uint16_t* out, const float* in, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = ane_lm::f32_to_f16(in[i]);
+}
+void ref_f16_to_f32_vec(float* out, const uint16_t* in, int64_t n) {
+    for (int64_t i = 0; i < n; i++) out[i] = ane_lm::f16_to_f32(in[i]);
+}
+
 void ref_rmsnorm(float* out, const float* x, const float* w, int dim, float eps) {
     ane_lm::rmsnorm(out, x, w, dim, eps);
 }

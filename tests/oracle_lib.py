@@ -64,6 +64,10 @@ def load_oracle() -> C.CDLL:
     lib.or_decode_attention.argtypes = [C.c_int, _p, _i64, _p, _i64, C.c_int, _p, _p, _i64,
                                         _p, _p, C.c_int, _i64, C.c_int, C.c_int, C.c_int]
     lib.or_kv_ring_advance.restype = C.c_int
+    lib.or_f32_to_f16_trunc.restype = C.c_uint16
+    lib.or_f32_to_f16_trunc.argtypes = [_f]
+    lib.or_ane_pack.argtypes = [C.c_int, _p, _p, _i64, _i64, C.c_int, C.c_int]
+    lib.or_ane_unpack.argtypes = [_p, _i64, _p, _i64, C.c_int, C.c_int]
     lib.or_kv_ring_advance.argtypes = [_p, _p, C.c_int]
     return lib
 
@@ -80,6 +84,8 @@ def load_ref():
     lib.ref_rope_row.argtypes = [_p, _p, C.c_int, C.c_int, _f]
     lib.ref_silu_vec_inplace.argtypes = [_p, C.c_int]
     lib.ref_softmax.argtypes = [_p, C.c_int]
+    lib.ref_f32_to_f16_vec.argtypes = [_p, _p, _i64]
+    lib.ref_f16_to_f32_vec.argtypes = [_p, _p, _i64]
     lib.ref_gqa_attention.argtypes = [_p, _p, _p, _p, C.c_int, C.c_int, C.c_int, C.c_int,
                                       C.c_int, C.c_int, C.c_int]
     lib.ref_sample_token.restype = C.c_int
@@ -202,6 +208,25 @@ class Oracle:
                                      _ptr(np.ascontiguousarray(start, np.int32)),
                                      _ptr(np.ascontiguousarray(length, np.int32)), cap, B, H, hk,
                                      hd)
+        return out
+
+    def ane_pack(self, x, round_mode=0, spatial=32, surface=None):
+        """x [tokens, channels] f32 -> surfaces [ceil(tokens/spatial), channels, spatial]
+        uint16 (fp16 bits); slots without a token keep `surface`'s values (zeros)."""
+        x = np.ascontiguousarray(x, np.float32)
+        t, c = x.shape
+        nsurf = (t + spatial - 1) // spatial
+        if surface is None:
+            surface = np.zeros((nsurf, c, spatial), np.uint16)
+        surface = np.ascontiguousarray(surface, np.uint16).copy()
+        self.lib.or_ane_pack(round_mode, _ptr(surface), _ptr(x), c, t, c, spatial)
+        return surface
+
+    def ane_unpack(self, surface, tokens, spatial=32):
+        surface = np.ascontiguousarray(surface, np.uint16)
+        c = surface.shape[1]
+        out = np.empty((tokens, c), np.float32)
+        self.lib.or_ane_unpack(_ptr(out), c, _ptr(surface), tokens, c, spatial)
         return out
 
     def kv_ring_advance(self, start, length, capacity):

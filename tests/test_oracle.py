@@ -243,3 +243,63 @@ def test_kv_ring_advance():
         slots.append(slot)
     assert slots == [0, 1, 2, 3, 0, 1, 2]
     assert (start, ln) == (3, 4)
+
+
+# ------------------------------------------- fp32 <-> fp16 at the ANE boundary
+def _f32_samples(n=1 << 20):
+    rng = np.random.default_rng(21)
+    bits = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    special = np.array([0, 0x80000000, 0x7F800000, 0xFF800000, 0x7FC00000, 0xFFC00001, 0x7F800001,
+                        0x33000000, 0x33000001, 0x387FC000, 0x38800000, 0x477FE000, 0x477FF000,
+                        0x477FEFFF, 0x00000001, 0x807FFFFF, 0x3F800000, 0x3F801000, 0x3F803000],
+                       np.uint32)
+    vals = (rng.standard_normal(n).astype(np.float32) * np.float32(100)).view(np.uint32)
+    return np.concatenate([special, bits, vals]).view(np.float32)
+
+
+def test_f32_to_f16_trunc_vs_reference(oracle, ref):
+    """The x86 packing conversion: bit-exact against the reference's
+    f32_to_f16 (include/ane_lm/common.h:58-71) over random bit patterns."""
+    x = _f32_samples()
+    want = np.empty(x.size, np.uint16)
+    ref.ref_f32_to_f16_vec(ptr(want), ptr(x), x.size)
+    got = oracle.ane_pack(x.reshape(1, -1), round_mode=1, spatial=1).ravel()
+    assert np.array_equal(got, want)
+
+
+def test_f32_to_f16_rne_vs_numpy(oracle):
+    """The arm64 packing conversion is IEEE round-to-nearest-even (numpy's
+    float32 -> float16); NaN becomes the quiet NaN 0x7E00 with its sign."""
+    x = _f32_samples()
+    got = oracle.ane_pack(x.reshape(1, -1), round_mode=0, spatial=1).ravel()
+    nan = np.isnan(x)
+    with np.errstate(over="ignore", invalid="ignore"):
+        want = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(got[~nan], want[~nan])
+    sign = (x.view(np.uint32)[nan] >> 16) & 0x8000
+    assert np.array_equal(got[nan], (0x7E00 | sign).astype(np.uint16))
+
+
+def test_f16_to_f32_vs_reference(oracle, ref):
+    """Unpacking widens exactly: all 65,536 halves, NaN payloads included,
+    bit-exact against the reference's f16_to_f32."""
+    h = np.arange(1 << 16, dtype=np.uint16)
+    want = np.empty(h.size, np.float32)
+    ref.ref_f16_to_f32_vec(ptr(want), ptr(h), h.size)
+    got = oracle.ane_unpack(h.reshape(1, -1, 1), tokens=1, spatial=1).ravel()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_ane_pack_layout(oracle):
+    """Token t -> surface t // 32, spatial slot t % 32, channel stride 32;
+    other slots keep their contents; unpack inverts pack on fp16 values."""
+    rng = np.random.default_rng(22)
+    t, c = 45, 7
+    x = rng.standard_normal((t, c)).astype(np.float16).astype(np.float32)
+    base = np.full((2, c, 32), 0xABCD, np.uint16)
+    s = oracle.ane_pack(x, surface=base)
+    assert s.shape == (2, c, 32)
+    assert np.array_equal(s[1, :, 13:], base[1, :, 13:])
+    assert np.array_equal(s[1, 3, 12], x[44, 3].astype(np.float16).view(np.uint16))
+    assert np.array_equal(s[0, 5, 31], x[31, 5].astype(np.float16).view(np.uint16))
+    assert np.array_equal(oracle.ane_unpack(s, t), x)
