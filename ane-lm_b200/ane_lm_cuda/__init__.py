@@ -47,6 +47,9 @@ _SIGS = {
     "ane_cuda_sample_rows": (_i, [_p, _i64, _i, _i64, _p, _p, _i64, _p, _f, _f, _i, _f, _p, _p]),
     "ane_cuda_write_ane_blobs": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
     "ane_cuda_convert_model": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
+    "ane_cuda_rmsnorm_gated": (_i, [_i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _f, _p]),
+    "ane_cuda_l2_normalize": (_i, [_i, _p, _i64, _i64, _i, _f, _p]),
+    "ane_cuda_bf16_to_f32": (_i, [_p, _p, _i64, _i, _p]),
     "ane_cuda_ane_pack": (_i, [_i, _p, _p, _i64, _i64, _i, _i, _p]),
     "ane_cuda_ane_unpack": (_i, [_p, _i64, _p, _i64, _i, _i, _p]),
     "ane_cuda_decode_attention_workspace_size": (_i64, [_i64, _i, _i, _i, _i]),
@@ -303,4 +306,38 @@ def ane_unpack(surface, tokens, spatial=32, out=None):
         out = torch.empty((tokens, channels), dtype=torch.float32, device=surface.device)
     _check("ane_unpack", lib().ane_cuda_ane_unpack(_ptr(out), out.stride(0), _ptr(surface), tokens,
                                                    channels, spatial, _stream(surface)))
+    return out
+
+
+def rmsnorm_gated(x, z, weight, out=None, eps=1e-6):
+    """((rmsnorm(x) * weight) / (1 + exp(-z))) * z over rows of x [rows, dim]."""
+    torch = _torch()
+    _cuda(x, z, weight)
+    rows, dim = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    _check("rmsnorm_gated", lib().ane_cuda_rmsnorm_gated(
+        _dt(x), _ptr(out), out.stride(0), _ptr(x), x.stride(0), _ptr(z), z.stride(0), _ptr(weight),
+        rows, dim, eps, _stream(x)))
+    return out
+
+
+def l2_normalize(x, scale=1.0):
+    """In place over rows of x [rows, dim]: x / sqrt(sum(x^2) + 1e-12) * scale."""
+    _cuda(x)
+    rows, dim = x.shape
+    _check("l2_normalize", lib().ane_cuda_l2_normalize(_dt(x), _ptr(x), x.stride(0), rows, dim,
+                                                       scale, _stream(x)))
+    return x
+
+
+def bf16_to_f32(bits, add_one=False, out=None):
+    """BF16 bits (int16 / uint16 / bfloat16 tensor) -> float32, optionally + 1."""
+    torch = _torch()
+    _cuda(bits)
+    bits = bits.contiguous()
+    if out is None:
+        out = torch.empty(bits.shape, dtype=torch.float32, device=bits.device)
+    _check("bf16_to_f32", lib().ane_cuda_bf16_to_f32(_ptr(out), _ptr(bits), bits.numel(),
+                                                     int(add_one), _stream(bits)))
     return out

@@ -62,6 +62,54 @@ void apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads, int he
 
 void softmax(float* x, int n) { note("softmax", ane_cuda_softmax_rows(x, 1, n, n, t_stream)); }
 
+void rmsnorm_gated(float* out, const float* x, const float* z, const float* weight, int dim) {
+    note("rmsnorm_gated", ane_cuda_rmsnorm_gated(ANE_CUDA_F32, out, dim, x, dim, z, dim, weight, 1,
+                                                 dim, 1e-6f, t_stream));
+}
+
+void l2_normalize(float* x, int dim) {
+    note("l2_normalize", ane_cuda_l2_normalize(ANE_CUDA_F32, x, dim, 1, dim, 1.0f, t_stream));
+}
+
+void gqa_attention(float* out, const float* q, const float* k_cache, const float* v_cache,
+                   int n_heads, int n_kv_heads, int head_dim, int q_head_stride,
+                   int cache_start, int cache_len, int cache_capacity) {
+    // The ring position goes to a per-thread device slot with the call: a
+    // copy from pageable memory is staged before cudaMemcpyAsync returns, and
+    // stream order keeps the slot until the kernel has read it.
+    thread_local int32_t* d_pos = nullptr;
+    thread_local int pos_dev = -1;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        note("gqa_attention", ANE_CUDA_ERR_CUDA);
+        return;
+    }
+    if (pos_dev != dev) {
+        if (d_pos) cudaFree(d_pos);
+        d_pos = nullptr;
+        pos_dev = -1;
+        if (cudaMalloc((void**)&d_pos, 2 * sizeof(int32_t)) != cudaSuccess) {
+            d_pos = nullptr;
+            note("gqa_attention", ANE_CUDA_ERR_CUDA);
+            return;
+        }
+        pos_dev = dev;
+    }
+    const int32_t pos[2] = {cache_start, cache_len};
+    cudaStream_t s = static_cast<cudaStream_t>(t_stream);
+    if (cudaMemcpyAsync(d_pos, pos, sizeof(pos), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+        note("gqa_attention", ANE_CUDA_ERR_CUDA);
+        return;
+    }
+    const int max_len = cache_len > 0 ? cache_len : 0;
+    note("gqa_attention",
+         ane_cuda_decode_attention(ANE_CUDA_F32, out, (int64_t)n_heads * head_dim, q,
+                                   (int64_t)n_heads * q_head_stride, q_head_stride, k_cache, v_cache,
+                                   (int64_t)cache_capacity * n_kv_heads * head_dim, d_pos, d_pos + 1,
+                                   cache_capacity, 1, n_heads, n_kv_heads, head_dim, max_len,
+                                   nullptr, 0, t_stream));
+}
+
 int sample_token(const float* logits, int vocab_size, const SamplingParams& params,
                  const std::vector<int>& recent_tokens) {
     int dev = 0;

@@ -46,6 +46,14 @@ void apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads,
                        int rot_dim, int pos, float theta,
                        const float* cos_row, const float* sin_row);
 void softmax(float* x, int n);
+void rmsnorm_gated(float* out, const float* x, const float* z, const float* weight, int dim);
+void l2_normalize(float* x, int dim);
+// gqa_attention (core/cpu_ops.h:55-58): q, k_cache, v_cache and out on the
+// device; the ring position is passed by value as in the reference.  Uses
+// the library-held workspace of the calling thread's stream.
+void gqa_attention(float* out, const float* q, const float* k_cache, const float* v_cache,
+                   int n_heads, int n_kv_heads, int head_dim, int q_head_stride,
+                   int cache_start, int cache_len, int cache_capacity);
 
 // ---- core/sampling.h -----------------------------------------------------
 struct SamplingParams {

@@ -171,6 +171,29 @@ ANE_CUDA_API int ane_cuda_sample_rows(const float* logits, int64_t rows, int voc
                          float repetition_penalty, int repetition_context,
                          float frequency_penalty, int32_t* out_tokens, void* stream);
 
+/* ---- row ops of the hybrid (linear-attention) layers ------------------------
+ * ane_cuda_rmsnorm_gated replaces rmsnorm_gated (core/cpu_ops.cpp:33-39,
+ * call site models/llm/qwen3_5.cpp:545-550) over rows:
+ *   out = ((rmsnorm(x) * w) / (1 + exp(-z))) * z      (eps 1e-6 there).
+ * ane_cuda_l2_normalize replaces l2_normalize (core/cpu_ops.cpp:106-111), in
+ * place over rows: x = (x * (1 / sqrtf(sum(x^2) + 1e-12))) * scale, scale
+ * being the q scaling that follows it (models/llm/qwen3_5.cpp:528-531; 1.0f
+ * leaves x as l2_normalize does).  fp32 math, the pinned sum order and exp;
+ * bit-exact against the reference in fp32. */
+ANE_CUDA_API int ane_cuda_rmsnorm_gated(int dtype, void* out, int64_t out_stride, const void* x,
+                                        int64_t x_stride, const void* z, int64_t z_stride,
+                                        const float* weight, int64_t rows, int dim, float eps,
+                                        void* stream);
+ANE_CUDA_API int ane_cuda_l2_normalize(int dtype, void* x, int64_t x_stride, int64_t rows, int dim,
+                                       float scale, void* stream);
+
+/* ---- norm-weight loading ----------------------------------------------------
+ * Replaces load_bf16_to_f32 (core/safetensors.cpp:264-279; add_one = 0) and
+ * the (1 + w) load_norm_weight of the hybrid model (:300-306; add_one = 1):
+ * out[i] = bf16_to_f32(in[i]) (+ 1.0f).  Bit-exact. */
+ANE_CUDA_API int ane_cuda_bf16_to_f32(float* out, const uint16_t* in, int64_t n, int add_one,
+                                      void* stream);
+
 /* ---- fp32 <-> fp16 packing at the ANE boundary ---------------------------
  * Replaces the element loops of ane_matvec (core/ane_runtime.cpp:611-653):
  * input channel c of a token goes to element c * spatial of the fp16

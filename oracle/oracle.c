@@ -299,6 +299,58 @@ void or_residual_rmsnorm(int dt, void* x, int64_t xs, const void* d, int64_t ds,
     free(v);
 }
 
+/* rmsnorm_gated, core/cpu_ops.cpp:33-39, over rows:
+ *   y = rmsnorm(x) * w                 (:25-31, eps as given; 1e-6 there)
+ *   y = y / (1 + exp(-z))              (mul_sigmoid_inplace, :16-23)
+ *   y = y * z                          (vDSP_vmul, :38)
+ * in fp32, rounded once to the row type at the end. */
+void or_rmsnorm_gated(int dt, void* out, int64_t os, const void* x, int64_t xs,
+                      const void* z, int64_t zs, const float* w, int64_t rows, int dim, float eps) {
+    float* v = (float*)malloc((size_t)dim * sizeof(float));
+    for (int64_t r = 0; r < rows; r++) {
+        for (int i = 0; i < dim; i++) v[i] = ld(x, dt, r * xs + i);
+        float ss = or_sumsq(v, dim, vec_of(dt));
+        float inv = 1.0f / sqrtf(ss / (float)dim + eps);
+        for (int i = 0; i < dim; i++) {
+            float zv = ld(z, dt, r * zs + i);
+            float y = v[i] * inv;
+            y = y * w[i];
+            float den = 1.0f + or_expf(-zv);
+            y = y / den;
+            y = y * zv;
+            st(out, dt, r * os + i, y);
+        }
+    }
+    free(v);
+}
+
+/* l2_normalize, core/cpu_ops.cpp:106-111, in place over rows:
+ * inv = 1 / sqrtf(sum(x^2) + 1e-12); x = x * inv; then x = x * scale (the
+ * q scaling of models/llm/qwen3_5.cpp:530-531; 1 leaves x unchanged). */
+void or_l2_normalize(int dt, void* x, int64_t xs, int64_t rows, int dim, float scale) {
+    float* v = (float*)malloc((size_t)dim * sizeof(float));
+    for (int64_t r = 0; r < rows; r++) {
+        for (int i = 0; i < dim; i++) v[i] = ld(x, dt, r * xs + i);
+        float inv = 1.0f / sqrtf(or_sumsq(v, dim, vec_of(dt)) + 1e-12f);
+        for (int i = 0; i < dim; i++) {
+            float y = v[i] * inv;
+            y = y * scale;
+            st(x, dt, r * xs + i, y);
+        }
+    }
+    free(v);
+}
+
+/* Norm-weight loading: load_bf16_to_f32 (core/safetensors.cpp:264-279,
+ * bf16_to_f32_vec) and, with add_one, the (1 + w) form of load_norm_weight
+ * (:300-306): w = bf16_to_f32(b) + 1.0f. */
+void or_bf16_to_f32_weights(float* out, const uint16_t* in, int64_t n, int add_one) {
+    for (int64_t i = 0; i < n; i++) {
+        float w = or_bf16_to_f32(in[i]);
+        out[i] = add_one ? w + 1.0f : w;
+    }
+}
+
 /* Per-head QK-norm (models/llm/qwen3.cpp:444-461, rmsnorm of each head with
  * q_norm / k_norm) followed by half-split RoPE (core/cpu_ops.cpp:43-54,
  * :56-66; models/llm/qwen3.cpp:17-52):

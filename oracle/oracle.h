@@ -67,6 +67,14 @@ void or_residual_rmsnorm(int dtype, void* x, int64_t x_stride,
                          void* out, int64_t out_stride,
                          const float* weight, int64_t rows, int dim, float eps);
 
+void or_rmsnorm_gated(int dtype, void* out, int64_t out_stride, const void* x, int64_t x_stride,
+                      const void* z, int64_t z_stride, const float* weight, int64_t rows, int dim,
+                      float eps);
+
+void or_l2_normalize(int dtype, void* x, int64_t x_stride, int64_t rows, int dim, float scale);
+
+void or_bf16_to_f32_weights(float* out, const uint16_t* in, int64_t n, int add_one);
+
 void or_qk_norm_rope(int dtype, void* q, void* k,
                      int64_t q_row_stride, int64_t k_row_stride,
                      int q_head_stride, int k_head_stride,

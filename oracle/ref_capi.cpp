@@ -89,6 +89,25 @@ int ref_sample_token(const float* logits, int vocab, float temperature, float re
     return tok;
 }
 
+/* rmsnorm_gated (core/cpu_ops.cpp:33-39) and l2_normalize (:106-111). */
+void ref_rmsnorm_gated(float* out, const float* x, const float* z, const float* w, int dim) {
+    ane_lm::rmsnorm_gated(out, x, z, w, dim);
+}
+void ref_l2_normalize(float* x, int dim) { ane_lm::l2_normalize(x, dim); }
+
+/* SafeTensors::load_norm_weight (core/safetensors.cpp:300-306) and
+ * load_bf16_to_f32 (:264-279) of one tensor; 0 on success. */
+int ref_load_weight(const char* path, const char* name, int64_t n, int norm, float* out) {
+    ane_lm::SafeTensors* sf = ane_lm::SafeTensors::open(path);
+    if (!sf) return -1;
+    float* w = norm ? sf->load_norm_weight(name, n) : sf->load_bf16_to_f32(name, n);
+    delete sf;
+    if (!w) return -2;
+    memcpy(out, w, (size_t)n * sizeof(float));
+    free(w);
+    return 0;
+}
+
 /* gqa_attention (core/cpu_ops.cpp:173-240) for one query token. */
 void ref_gqa_attention(float* out, const float* q, const float* k_cache, const float* v_cache,
                        int n_heads, int n_kv_heads, int head_dim, int q_head_stride,

@@ -51,6 +51,9 @@ int main(int argc, char** argv) {
     auto logits = get<float>(in, vocab);
     auto hist = get<int>(in, 300);
     auto bf = get<uint16_t>(in, 1000);
+    const int cap = 300, a_start = 250, a_len = 290;
+    auto kc = get<float>(in, (size_t)cap * nkv * hd);
+    auto vc = get<float>(in, (size_t)cap * nkv * hd);
 
     cudaStream_t s;
     cudaStreamCreate(&s);
@@ -106,6 +109,32 @@ int main(int argc, char** argv) {
     cu::bf16_to_f16_vec(dh, db, (int)bf.size());
     cudaStreamSynchronize(s);
     put(out, to_host(dh, bf.size()));
+
+    // hybrid-model row ops, one head per call as models/llm/qwen3_5.cpp:528-550
+    float* dgx = to_dev(x);
+    float* dgz = to_dev(z);
+    float* dgo = nullptr;
+    cudaMalloc(&dgo, dim * sizeof(float));
+    for (int h = 0; h < dim / hd; h++) cu::rmsnorm_gated(dgo + h * hd, dgx + h * hd, dgz + h * hd, dw, hd);
+    cudaStreamSynchronize(s);
+    put(out, to_host(dgo, dim));
+    float* dl2 = to_dev(qk);
+    for (int h = 0; h < nq + nkv; h++) cu::l2_normalize(dl2 + h * hd, hd);
+    cudaStreamSynchronize(s);
+    put(out, to_host(dl2, qk.size()));
+
+    // gqa_attention over a wrapped ring (core/cpu_ops.cpp:173-240)
+    float* dkc = to_dev(kc);
+    float* dvc = to_dev(vc);
+    float* dqa = to_dev(qk);
+    float* dao = nullptr;
+    cudaMalloc(&dao, nq * hd * sizeof(float));
+    cu::gqa_attention(dao, dqa, dkc, dvc, nq, nkv, hd, hd, a_start, a_len, cap);
+    cudaStreamSynchronize(s);
+    put(out, to_host(dao, (size_t)nq * hd));
+    cu::gqa_attention(dao, dqa, dkc, dvc, nq, nkv, hd, hd, 7, 0, cap);  // empty cache -> zeros
+    cudaStreamSynchronize(s);
+    put(out, to_host(dao, (size_t)nq * hd));
 
     // a failing call: reported through last_status, the process continues
     cu::rmsnorm(dx, dx, nullptr, dim, 1e-6f);

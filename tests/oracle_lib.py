@@ -64,6 +64,9 @@ def load_oracle() -> C.CDLL:
     lib.or_decode_attention.argtypes = [C.c_int, _p, _i64, _p, _i64, C.c_int, _p, _p, _i64,
                                         _p, _p, C.c_int, _i64, C.c_int, C.c_int, C.c_int]
     lib.or_kv_ring_advance.restype = C.c_int
+    lib.or_rmsnorm_gated.argtypes = [C.c_int, _p, _i64, _p, _i64, _p, _i64, _p, _i64, C.c_int, _f]
+    lib.or_l2_normalize.argtypes = [C.c_int, _p, _i64, _i64, C.c_int, _f]
+    lib.or_bf16_to_f32_weights.argtypes = [_p, _p, _i64, C.c_int]
     lib.or_f32_to_f16_trunc.restype = C.c_uint16
     lib.or_f32_to_f16_trunc.argtypes = [_f]
     lib.or_ane_pack.argtypes = [C.c_int, _p, _p, _i64, _i64, C.c_int, C.c_int]
@@ -84,6 +87,10 @@ def load_ref():
     lib.ref_rope_row.argtypes = [_p, _p, C.c_int, C.c_int, _f]
     lib.ref_silu_vec_inplace.argtypes = [_p, C.c_int]
     lib.ref_softmax.argtypes = [_p, C.c_int]
+    lib.ref_rmsnorm_gated.argtypes = [_p, _p, _p, _p, C.c_int]
+    lib.ref_l2_normalize.argtypes = [_p, C.c_int]
+    lib.ref_load_weight.restype = C.c_int
+    lib.ref_load_weight.argtypes = [C.c_char_p, C.c_char_p, _i64, C.c_int, _p]
     lib.ref_f32_to_f16_vec.argtypes = [_p, _p, _i64]
     lib.ref_f16_to_f32_vec.argtypes = [_p, _p, _i64]
     lib.ref_gqa_attention.argtypes = [_p, _p, _p, _p, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -208,6 +215,29 @@ class Oracle:
                                      _ptr(np.ascontiguousarray(start, np.int32)),
                                      _ptr(np.ascontiguousarray(length, np.int32)), cap, B, H, hk,
                                      hd)
+        return out
+
+    def rmsnorm_gated(self, x, z, w, eps=1e-6):
+        dt = dtype_code(x)
+        x = np.ascontiguousarray(x)
+        z = np.ascontiguousarray(z, x.dtype)
+        rows, dim = x.shape
+        out = np.empty_like(x)
+        self.lib.or_rmsnorm_gated(dt, _ptr(out), dim, _ptr(x), dim, _ptr(z), dim,
+                                  _ptr(np.ascontiguousarray(w, np.float32)), rows, dim, eps)
+        return out
+
+    def l2_normalize(self, x, scale=1.0):
+        dt = dtype_code(x)
+        x = np.ascontiguousarray(x).copy()
+        rows, dim = x.shape
+        self.lib.or_l2_normalize(dt, _ptr(x), dim, rows, dim, scale)
+        return x
+
+    def bf16_to_f32_weights(self, b, add_one):
+        b = np.ascontiguousarray(b, np.uint16)
+        out = np.empty(b.shape, np.float32)
+        self.lib.or_bf16_to_f32_weights(_ptr(out), _ptr(b), b.size, int(add_one))
         return out
 
     def ane_pack(self, x, round_mode=0, spatial=32, surface=None):

@@ -51,9 +51,12 @@ def test_reference_signature_layer(checker, oracle):
     logits = (rng.standard_normal(vocab) * 3).astype(np.float32)
     hist = rng.integers(0, vocab, 300).astype(np.int32)
     bf = rng.integers(0, 65536, 1000).astype(np.uint16)
+    cap = 300
+    kc = rng.standard_normal((cap, nkv, hd)).astype(np.float32)
+    vc = rng.standard_normal((cap, nkv, hd)).astype(np.float32)
     inp, outp = d / "in.bin", d / "out.bin"
     with open(inp, "wb") as f:
-        for a in (x, w, qk, cosr, sinr, g, z, logits, hist, bf):
+        for a in (x, w, qk, cosr, sinr, g, z, logits, hist, bf, kc, vc):
             f.write(a.tobytes())
     subprocess.run([exe, str(inp), str(outp)], check=True, timeout=120)
     raw = outp.read_bytes()
@@ -96,6 +99,16 @@ def test_reference_signature_layer(checker, oracle):
     assert toks[5] == oracle.sample_rows(logits[None], u[4:5])[0]
     # bf16_to_f16_vec
     assert np.array_equal(take(np.uint16, bf.size), oracle.bf16_to_f16(bf))
+    # rmsnorm_gated per head (x as 16 heads of 128, z's first 2048, w's first 128)
+    want = oracle.rmsnorm_gated(x.reshape(-1, hd), z[:dim].reshape(-1, hd), w[:hd]).ravel()
+    assert np.array_equal(take(np.float32, dim), want)
+    # l2_normalize per head of qk
+    assert np.array_equal(take(np.float32, qk.size), oracle.l2_normalize(qk.reshape(-1, hd)).ravel())
+    # gqa_attention: q = the first 16 heads of qk, ring start 250, 290 keys of 300
+    q = qk[:nq * hd].reshape(1, nq, hd)
+    want = oracle.decode_attention(q, kc[None], vc[None], [250], [290])[0].ravel()
+    assert np.array_equal(take(np.float32, nq * hd), want)
+    assert not np.any(take(np.float32, nq * hd))
     # a failing call reports through last_status() and the process carries on
     assert take(np.int32, 1)[0] == 1
     assert off == len(raw)

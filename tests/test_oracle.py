@@ -303,3 +303,49 @@ def test_ane_pack_layout(oracle):
     assert np.array_equal(s[1, 3, 12], x[44, 3].astype(np.float16).view(np.uint16))
     assert np.array_equal(s[0, 5, 31], x[31, 5].astype(np.float16).view(np.uint16))
     assert np.array_equal(oracle.ane_unpack(s, t), x)
+
+
+# ------------------------------------------------------ hybrid-model row ops
+@pytest.mark.parametrize("dim", [128, 64, 100])
+def test_rmsnorm_gated_vs_reference(oracle, ref, dim):
+    """rmsnorm_gated (core/cpu_ops.cpp:33-39): bit-exact, fp32."""
+    rng = np.random.default_rng(dim)
+    rows = 6
+    x = rng.standard_normal((rows, dim)).astype(np.float32) * 3
+    z = rng.standard_normal((rows, dim)).astype(np.float32) * 4
+    z[0, :4] = [-90.0, 90.0, -0.0, 40.0]
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    got = oracle.rmsnorm_gated(x, z, w)
+    for r in range(rows):
+        want = np.empty(dim, np.float32)
+        ref.ref_rmsnorm_gated(ptr(want), ptr(x[r]), ptr(z[r]), ptr(w), dim)
+        assert np.array_equal(got[r].view(np.uint32), want.view(np.uint32)), r
+
+
+@pytest.mark.parametrize("dim", [128, 64, 100, 4096])
+def test_l2_normalize_vs_reference(oracle, ref, dim):
+    """l2_normalize (core/cpu_ops.cpp:106-111): bit-exact, fp32, a zero row too."""
+    rng = np.random.default_rng(dim + 1)
+    x = rng.standard_normal((5, dim)).astype(np.float32) * 2
+    x[3] = 0.0
+    got = oracle.l2_normalize(x)
+    for r in range(5):
+        want = x[r].copy()
+        ref.ref_l2_normalize(ptr(want), dim)
+        assert np.array_equal(got[r].view(np.uint32), want.view(np.uint32)), r
+
+
+def test_norm_weight_load_vs_reference(oracle, ref, tmp_path):
+    """load_bf16_to_f32 and the (1 + w) load_norm_weight (core/safetensors.cpp:
+    264-306) of a BF16 tensor: bit-exact, specials included."""
+    from safetensors_util import write_safetensors
+    rng = np.random.default_rng(9)
+    b = rng.integers(0, 1 << 16, 4096, dtype=np.uint64).astype(np.uint16)
+    b[:6] = [0x0000, 0x8000, 0x7F80, 0xFF80, 0x7FC0, 0x3F80]
+    path = str(tmp_path / "w.safetensors")
+    write_safetensors(path, [("model.norm.weight", "BF16", b)])
+    for norm in (0, 1):
+        want = np.empty(4096, np.float32)
+        assert ref.ref_load_weight(path.encode(), b"model.norm.weight", 4096, norm, ptr(want)) == 0
+        got = oracle.bf16_to_f32_weights(b, norm)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), norm
