@@ -47,6 +47,8 @@ _SIGS = {
     "ane_cuda_sample_rows": (_i, [_p, _i64, _i, _i64, _p, _p, _i64, _p, _f, _f, _i, _f, _p, _p]),
     "ane_cuda_write_ane_blobs": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
     "ane_cuda_convert_model": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_i64), _p]),
+    "ane_cuda_qk_norm_rope_kv": (_i, [_i, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _i,
+                                      _p, _p, _p, _p, _p, _i64, _p, _i, _i64, _f, _f, _p]),
     "ane_cuda_rmsnorm_gated": (_i, [_i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _f, _p]),
     "ane_cuda_l2_normalize": (_i, [_i, _p, _i64, _i64, _i, _f, _p]),
     "ane_cuda_bf16_to_f32": (_i, [_p, _p, _i64, _i, _p]),
@@ -341,3 +343,23 @@ def bf16_to_f32(bits, add_one=False, out=None):
     _check("bf16_to_f32", lib().ane_cuda_bf16_to_f32(_ptr(out), _ptr(bits), bits.numel(),
                                                      int(add_one), _stream(bits)))
     return out
+
+
+def qk_norm_rope_kv(qkv, q_weight, k_weight, positions, n_q_heads, n_kv_heads, head_dim,
+                    k_cache, v_cache, slots, theta=1e6, eps=1e-6):
+    """qk_norm_rope on qkv [rows, (n_q + 2 n_kv) * head_dim] in place, and row r's k heads
+    (after RoPE) and v heads written to ring slot slots[r] of k_cache / v_cache:
+    [cap, n_kv, head_dim] shared by all rows, or [rows, cap, n_kv, head_dim] per row."""
+    _cuda(qkv, q_weight, k_weight, positions, k_cache, v_cache, slots)
+    rows, width = qkv.shape
+    es = qkv.element_size()
+    base = qkv.data_ptr()
+    k = C.c_void_p(base + n_q_heads * head_dim * es)
+    v = C.c_void_p(base + (n_q_heads + n_kv_heads) * head_dim * es)
+    crs = k_cache.stride(0) if k_cache.dim() == 4 else 0
+    capacity = k_cache.shape[-3]
+    _check("qk_norm_rope_kv", lib().ane_cuda_qk_norm_rope_kv(
+        _dt(qkv), _ptr(qkv), k, v, qkv.stride(0), qkv.stride(0), qkv.stride(0), head_dim, head_dim,
+        head_dim, n_q_heads, n_kv_heads, head_dim, _ptr(q_weight), _ptr(k_weight), _ptr(positions),
+        _ptr(k_cache), _ptr(v_cache), crs, _ptr(slots), capacity, rows, theta, eps, _stream(qkv)))
+    return qkv

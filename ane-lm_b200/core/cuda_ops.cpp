@@ -71,6 +71,19 @@ void l2_normalize(float* x, int dim) {
     note("l2_normalize", ane_cuda_l2_normalize(ANE_CUDA_F32, x, dim, 1, dim, 1.0f, t_stream));
 }
 
+int kv_ring_advance(int* start, int* len, int capacity) {
+    int slot;
+    if (*len < capacity) {
+        slot = *start + *len;
+        if (slot >= capacity) slot -= capacity;
+        (*len)++;
+    } else {
+        slot = *start;
+        if (++*start >= capacity) *start = 0;
+    }
+    return slot;
+}
+
 void gqa_attention(float* out, const float* q, const float* k_cache, const float* v_cache,
                    int n_heads, int n_kv_heads, int head_dim, int q_head_stride,
                    int cache_start, int cache_len, int cache_capacity) {

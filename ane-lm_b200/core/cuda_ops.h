@@ -55,6 +55,12 @@ void gqa_attention(float* out, const float* q, const float* k_cache, const float
                    int n_heads, int n_kv_heads, int head_dim, int q_head_stride,
                    int cache_start, int cache_len, int cache_capacity);
 
+// The KV ring bookkeeping of the decode step (models/llm/qwen3.cpp:475-484):
+// the slot the new token's k / v rows go to (qk_norm_rope_kv's slots[r]);
+// start and len advance as in the reference (fill, then overwrite the
+// oldest slot).  Host only.
+int kv_ring_advance(int* start, int* len, int capacity);
+
 // ---- core/sampling.h -----------------------------------------------------
 struct SamplingParams {
     float temperature = 0.6f;

@@ -43,6 +43,18 @@ struct QkArgs {
     float eps;
     const float* cos_row;      // generic path only: caller tables
     const float* sin_row;
+    // KV-cache write (row kernel, KV = true): row r's k heads after norm and
+    // RoPE, and its v heads unchanged, go to ring slot slots[r] (< 0: none)
+    // of the caches [slot][n_kv][head_dim] at cache + r * cache_row_stride.
+    const void* v;
+    int64_t v_row_stride;
+    int v_head_stride;
+    void* k_cache;
+    void* v_cache;
+    int64_t cache_row_stride;
+    const int32_t* slots;
+    int cache_capacity;        // slots outside [0, capacity) write nothing and raise a flag
+    unsigned int* flags;
 };
 
 // One warp per row.  The row's heads stream through a ring of D register
@@ -54,8 +66,8 @@ struct QkArgs {
 // and the norm weights are staged once per CTA in shared memory.
 constexpr int kRowWarps = 4;
 
-template <typename T, int GL, int D>
-__global__ void __launch_bounds__(kRowWarps * kWarp, 8)
+template <typename T, int GL, int D, bool KV>
+__global__ void __launch_bounds__(kRowWarps * kWarp, KV ? 4 : 8)
 qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim) {
     using S = typename T::storage;
     constexpr int V = T::kVec;
@@ -77,12 +89,28 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
     if (row >= a.rows) return;
     const int g = lane / GL;  // head slot of this lane
     const int l = lane % GL;  // lane within the head group
-    const int nq = a.n_q, nh = a.n_q + a.n_kv;
+    const int nq = a.n_q, nqk = a.n_q + a.n_kv;
+    const int nh = KV ? nqk + a.n_kv : nqk;  // with KV the v heads follow, copy only
     const int nit = (nh + HPW - 1) / HPW;
     S* const qrow = (S*)a.q + row * a.q_row_stride;
     S* const krow = (S*)a.k + row * a.k_row_stride;
     const int qhs = a.q_head_stride, khs = a.k_head_stride;
-    auto head_ptr = [&](int h) -> S* { return h < nq ? qrow + h * qhs : krow + (h - nq) * khs; };
+    auto head_ptr = [&](int h) -> S* {
+        if (KV && h >= nqk) return (S*)a.v + row * a.v_row_stride + (int64_t)(h - nqk) * a.v_head_stride;
+        return h < nq ? qrow + h * qhs : krow + (h - nq) * khs;
+    };
+    int slot = -1;
+    if constexpr (KV) {
+        slot = __ldg(a.slots + row);
+        if (slot >= a.cache_capacity) {
+            if (lane == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_BAD_CACHE);
+            slot = -1;
+        }
+    }
+    // cache row of kv head j in this row's slot
+    auto cache_ptr = [&](void* cache, int j) -> S* {
+        return (S*)cache + row * a.cache_row_stride + ((int64_t)slot * a.n_kv + j) * (2 * HALF);
+    };
 
     uint4 lo[D], hi[D];
 #pragma unroll
@@ -123,6 +151,12 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
             if (it0 + d >= nit) break;  // warp-uniform
             const int h = (it0 + d) * HPW + g;
             const bool live = h < nh;
+            const bool vhead = KV && h >= nqk;  // copied bit for bit, no norm / RoPE
+            uint4 raw_lo, raw_hi;
+            if constexpr (KV) {
+                raw_lo = lo[d];
+                raw_hi = hi[d];
+            }
             float x0[V], x1[V];
             if (live) {
                 unpack<T>(lo[d], x0);
@@ -147,7 +181,7 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
                 const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
                 const float* w = s_w[h < nq ? 0 : 1];
 #pragma unroll
-                for (int q4 = 0; q4 < V / 4; q4++) {
+                for (int q4 = 0; q4 < (vhead ? 0 : V / 4); q4++) {
                     const float4 t0 = reinterpret_cast<const float4*>(w + l * V)[q4];
                     const float4 t1 = reinterpret_cast<const float4*>(w + HALF + l * V)[q4];
                     const float w0[4] = {t0.x, t0.y, t0.z, t0.w};
@@ -159,16 +193,28 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
                     }
                 }
             }
-            if (live) {
+            if (vhead) {
+                if (live && slot >= 0) {
+                    S* c = cache_ptr(a.v_cache, h - nqk);
+                    st_stream(c + l * V, raw_lo);
+                    st_stream(c + HALF + l * V, raw_hi);
+                }
+            } else if (live) {
                 float y0[V], y1[V];
 #pragma unroll
                 for (int e = 0; e < V; e++) {
                     y0[e] = __fsub_rn(__fmul_rn(x0[e], cs[e]), __fmul_rn(x1[e], sn[e]));
                     y1[e] = __fadd_rn(__fmul_rn(x1[e], cs[e]), __fmul_rn(x0[e], sn[e]));
                 }
+                const uint4 p0 = pack<T>(y0), p1 = pack<T>(y1);
                 S* q = head_ptr(h);
-                st_stream(q + l * V, pack<T>(y0));
-                st_stream(q + HALF + l * V, pack<T>(y1));
+                st_stream(q + l * V, p0);
+                st_stream(q + HALF + l * V, p1);
+                if (KV && h >= nq && slot >= 0) {  // k head after RoPE: also into the cache
+                    S* c = cache_ptr(a.k_cache, h - nq);
+                    st_stream(c + l * V, p0);
+                    st_stream(c + HALF + l * V, p1);
+                }
             }
         }
     }
@@ -246,7 +292,7 @@ static int ilog2_exact(int v) {
 }
 
 template <typename T>
-static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s) {
+static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s, bool kv) {
     constexpr int V = T::kVec;
     const int es = (int)sizeof(typename T::storage);
     const int nh = a.n_q + a.n_kv;
@@ -256,10 +302,23 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s) {
                 gl_log2 >= 0 && nchunk <= 32 && is_aligned(a.q, 16) && is_aligned(a.k, 16) &&
                 (a.q_row_stride * es) % 16 == 0 && (a.k_row_stride * es) % 16 == 0 &&
                 (a.q_head_stride * es) % 16 == 0 && (a.k_head_stride * es) % 16 == 0;
+    if (kv) {
+        const bool ok = fast && is_aligned(a.v, 16) && is_aligned(a.k_cache, 16) &&
+                        is_aligned(a.v_cache, 16) && (a.v_row_stride * es) % 16 == 0 &&
+                        (a.v_head_stride * es) % 16 == 0 && (a.cache_row_stride * es) % 16 == 0;
+        if (!ok)
+            return fail(ANE_CUDA_ERR_UNSUPPORTED,
+                        "qk_norm_rope_kv: needs head_dim / %d a power of two <= 32 and 16-byte aligned "
+                        "rows, heads and caches", V);
+    }
     if (fast) {
         const unsigned blocks = (unsigned)((a.rows + kRowWarps - 1) / kRowWarps);
         const bool pow2 = (a.head_dim & (a.head_dim - 1)) == 0;
-#define ANE_QK_ROW(GLV) qk_norm_rope_row_kernel<T, GLV, 2><<<blocks, kRowWarps * kWarp, 0, s>>>(a, fr, pow2)
+#define ANE_QK_ROW(GLV)                                                                          \
+    do {                                                                                          \
+        if (kv) qk_norm_rope_row_kernel<T, GLV, 2, true><<<blocks, kRowWarps * kWarp, 0, s>>>(a, fr, pow2); \
+        else qk_norm_rope_row_kernel<T, GLV, 2, false><<<blocks, kRowWarps * kWarp, 0, s>>>(a, fr, pow2);   \
+    } while (0)
         switch (gl_log2) {
             case 0: ANE_QK_ROW(1); break;
             case 1: ANE_QK_ROW(2); break;
@@ -279,12 +338,12 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s) {
     return check_launch("qk_norm_rope");
 }
 
-static int run_qk(int dtype, const QkArgs& a, float theta, cudaStream_t s) {
+static int run_qk(int dtype, const QkArgs& a, float theta, cudaStream_t s, bool kv = false) {
     RopeFreq fr;
     make_freq(&fr, a.rot_dim, theta);
-    if (dtype == ANE_CUDA_F32) return launch_qk<F32>(a, fr, s);
-    if (dtype == ANE_CUDA_F16) return launch_qk<F16>(a, fr, s);
-    return launch_qk<BF16>(a, fr, s);
+    if (dtype == ANE_CUDA_F32) return launch_qk<F32>(a, fr, s, kv);
+    if (dtype == ANE_CUDA_F16) return launch_qk<F16>(a, fr, s, kv);
+    return launch_qk<BF16>(a, fr, s, kv);
 }
 
 static int validate(const char* fn, const QkArgs& a) {
@@ -323,6 +382,31 @@ int ane_cuda_qk_norm_rope(int dtype, void* q, void* k, int64_t q_row_stride,
     if (rows == 0) return ANE_CUDA_OK;
     if (!positions) return fail(ANE_CUDA_ERR_INVALID_ARG, "qk_norm_rope: positions is NULL");
     return run_qk(dtype, a, theta, as_stream(stream));
+}
+
+int ane_cuda_qk_norm_rope_kv(int dtype, void* q, void* k, const void* v, int64_t q_row_stride,
+                             int64_t k_row_stride, int64_t v_row_stride, int q_head_stride,
+                             int k_head_stride, int v_head_stride, int n_q_heads, int n_kv_heads,
+                             int head_dim, const float* q_weight, const float* k_weight,
+                             const int32_t* positions, void* k_cache, void* v_cache,
+                             int64_t cache_row_stride, const int32_t* slots, int cache_capacity,
+                             int64_t rows, float theta, float eps, void* stream) {
+    using namespace ane;
+    if (!valid_dtype(dtype)) return fail(ANE_CUDA_ERR_INVALID_ARG, "qk_norm_rope_kv: bad dtype %d", dtype);
+    QkArgs a{q, k, q_row_stride, k_row_stride, q_head_stride, k_head_stride, n_q_heads, n_kv_heads,
+             head_dim, head_dim, q_weight, k_weight, positions, 0, rows, eps, nullptr, nullptr,
+             v, v_row_stride, v_head_stride, k_cache, v_cache, cache_row_stride, slots,
+             cache_capacity, status_flags_device()};
+    int st = validate("qk_norm_rope_kv", a);
+    if (st) return st;
+    if (rows == 0) return ANE_CUDA_OK;
+    if (n_kv_heads <= 0 || !positions || !v || !k_cache || !v_cache || !slots)
+        return fail(ANE_CUDA_ERR_INVALID_ARG, "qk_norm_rope_kv: null pointer or no kv heads");
+    if (cache_row_stride < 0 || cache_capacity <= 0 ||
+        (cache_row_stride > 0 && cache_row_stride < (int64_t)cache_capacity * n_kv_heads * head_dim))
+        return fail(ANE_CUDA_ERR_INVALID_ARG, "qk_norm_rope_kv: cache_row_stride %lld capacity %d",
+                    (long long)cache_row_stride, cache_capacity);
+    return run_qk(dtype, a, theta, as_stream(stream), true);
 }
 
 int ane_cuda_apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads, int head_dim,

@@ -125,6 +125,28 @@ ANE_CUDA_API int ane_cuda_qk_norm_rope(int dtype, void* q, void* k, int64_t q_ro
                           const int32_t* positions, int64_t rows, float theta, float eps,
                           void* stream);
 
+/* Per-head QK-norm + RoPE with the KV-cache write of the decode step
+ * (models/llm/qwen3.cpp:440-488): as ane_cuda_qk_norm_rope (rot_dim =
+ * head_dim), and in the same pass row r's k heads after RoPE and its v
+ * heads (v + r*v_row_stride + j*v_head_stride, unchanged) are written to
+ * ring slot slots[r] of the caches [slot][n_kv_heads][head_dim] at
+ * k_cache / v_cache + r*cache_row_stride (0 when all rows are tokens of one
+ * sequence; a per-sequence cache stride for a batch of decode rows);
+ * slots[r] < 0 writes no cache row; slots[r] >= cache_capacity writes none
+ * and sets ANE_CUDA_FLAG_BAD_CACHE.  The slot follows the reference's ring
+ * bookkeeping (:475-484), done by the caller.  Needs the row kernel's
+ * shapes: head_dim / (16 / element size) a power of two <= 32, 16-byte
+ * aligned rows, heads and caches (ANE_CUDA_ERR_UNSUPPORTED otherwise). */
+ANE_CUDA_API int ane_cuda_qk_norm_rope_kv(int dtype, void* q, void* k, const void* v,
+                                          int64_t q_row_stride, int64_t k_row_stride,
+                                          int64_t v_row_stride, int q_head_stride,
+                                          int k_head_stride, int v_head_stride, int n_q_heads,
+                                          int n_kv_heads, int head_dim, const float* q_weight,
+                                          const float* k_weight, const int32_t* positions,
+                                          void* k_cache, void* v_cache, int64_t cache_row_stride,
+                                          const int32_t* slots, int cache_capacity, int64_t rows,
+                                          float theta, float eps, void* stream);
+
 /* The single-position form with caller-supplied cos/sin rows, exactly
  * apply_rope_cached (core/cpu_ops.h:25-28) on fp32 device data.  When
  * cos_row or sin_row is NULL, cos/sin are computed in registers (half-split

@@ -392,6 +392,27 @@ void or_qk_norm_rope(int dt, void* q, void* k, int64_t qrs, int64_t krs,
     free(inv_freq); free(cs); free(sn); free(v);
 }
 
+/* QK-norm + RoPE followed by the KV-cache write of the decode step,
+ * models/llm/qwen3.cpp:470-488: after RoPE, the token's k heads and its v
+ * heads are copied (memcpy) into ring slot slots[r] of the caches
+ * [slot][n_kv][hd] at cache + r * crs; slots[r] < 0 copies nothing. */
+void or_qk_norm_rope_kv(int dt, void* q, void* k, const void* v, int64_t qrs, int64_t krs,
+                        int64_t vrs, int qhs, int khs, int vhs, int nq, int nkv, int hd,
+                        const float* qw, const float* kw, const int32_t* pos, void* k_cache,
+                        void* v_cache, int64_t crs, const int32_t* slots, int64_t rows,
+                        float theta, float eps) {
+    or_qk_norm_rope(dt, q, k, qrs, krs, qhs, khs, nq, nkv, hd, hd, qw, kw, pos, rows, theta, eps);
+    const size_t es = dt == OR_F32 ? 4 : 2;
+    for (int64_t r = 0; r < rows; r++) {
+        if (slots[r] < 0) continue;
+        for (int j = 0; j < nkv; j++) {
+            const int64_t dst = (r * crs + ((int64_t)slots[r] * nkv + j) * hd) * (int64_t)es;
+            memcpy((char*)k_cache + dst, (const char*)k + (r * krs + (int64_t)j * khs) * (int64_t)es, hd * es);
+            memcpy((char*)v_cache + dst, (const char*)v + (r * vrs + (int64_t)j * vhs) * (int64_t)es, hd * es);
+        }
+    }
+}
+
 /* SiLU-gated activation: silu_vec_inplace (core/cpu_ops.cpp:7-14,
  * x / (1 + exp(-x))) times up, the gate*sigmoid(gate)*up of the fused FFN
  * (core/ane_runtime.cpp:393-395) evaluated in fp32. */

@@ -83,6 +83,14 @@ void or_qk_norm_rope(int dtype, void* q, void* k,
                      const int32_t* positions, int64_t rows,
                      float theta, float eps);
 
+void or_qk_norm_rope_kv(int dtype, void* q, void* k, const void* v, int64_t q_row_stride,
+                        int64_t k_row_stride, int64_t v_row_stride, int q_head_stride,
+                        int k_head_stride, int v_head_stride, int n_q_heads, int n_kv_heads,
+                        int head_dim, const float* q_weight, const float* k_weight,
+                        const int32_t* positions, void* k_cache, void* v_cache,
+                        int64_t cache_row_stride, const int32_t* slots, int64_t rows,
+                        float theta, float eps);
+
 void or_silu_mul(int dtype, void* out, int64_t out_stride,
                  const void* gate, int64_t gate_stride,
                  const void* up, int64_t up_stride,

@@ -136,6 +136,14 @@ int main(int argc, char** argv) {
     cudaStreamSynchronize(s);
     put(out, to_host(dao, (size_t)nq * hd));
 
+    // KV ring bookkeeping: 7 appends into a ring of 4
+    std::vector<int> ring;
+    int rs = 0, rl = 0;
+    for (int i = 0; i < 7; i++) ring.push_back(cu::kv_ring_advance(&rs, &rl, 4));
+    ring.push_back(rs);
+    ring.push_back(rl);
+    put(out, ring);
+
     // a failing call: reported through last_status, the process continues
     cu::rmsnorm(dx, dx, nullptr, dim, 1e-6f);
     std::vector<int> st = {cu::last_status()};

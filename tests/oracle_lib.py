@@ -64,6 +64,9 @@ def load_oracle() -> C.CDLL:
     lib.or_decode_attention.argtypes = [C.c_int, _p, _i64, _p, _i64, C.c_int, _p, _p, _i64,
                                         _p, _p, C.c_int, _i64, C.c_int, C.c_int, C.c_int]
     lib.or_kv_ring_advance.restype = C.c_int
+    lib.or_qk_norm_rope_kv.argtypes = [C.c_int, _p, _p, _p, _i64, _i64, _i64, C.c_int, C.c_int,
+                                       C.c_int, C.c_int, C.c_int, C.c_int, _p, _p, _p, _p, _p,
+                                       _i64, _p, _i64, _f, _f]
     lib.or_rmsnorm_gated.argtypes = [C.c_int, _p, _i64, _p, _i64, _p, _i64, _p, _i64, C.c_int, _f]
     lib.or_l2_normalize.argtypes = [C.c_int, _p, _i64, _i64, C.c_int, _f]
     lib.or_bf16_to_f32_weights.argtypes = [_p, _p, _i64, C.c_int]
@@ -216,6 +219,27 @@ class Oracle:
                                      _ptr(np.ascontiguousarray(length, np.int32)), cap, B, H, hk,
                                      hd)
         return out
+
+    def qk_norm_rope_kv(self, qkv, nq, nkv, hd, qw, kw, pos, theta, k_cache, v_cache, slots,
+                        per_row_cache=False, eps=1e-6):
+        """qkv [rows, (nq + 2 nkv) hd]; caches [cap, nkv, hd] shared by all rows, or
+        [rows, cap, nkv, hd] with per_row_cache.  Returns (qkv, k_cache, v_cache) copies."""
+        dt = dtype_code(qkv)
+        qkv = np.ascontiguousarray(qkv).copy()
+        kc = np.ascontiguousarray(k_cache).copy()
+        vc = np.ascontiguousarray(v_cache).copy()
+        rows, width = qkv.shape
+        es = qkv.itemsize
+        base = qkv.ctypes.data
+        crs = (kc.size // rows) if per_row_cache else 0
+        self.lib.or_qk_norm_rope_kv(dt, C.c_void_p(base), C.c_void_p(base + nq * hd * es),
+                                    C.c_void_p(base + (nq + nkv) * hd * es), width, width, width,
+                                    hd, hd, hd, nq, nkv, hd,
+                                    _ptr(np.ascontiguousarray(qw, np.float32)),
+                                    _ptr(np.ascontiguousarray(kw, np.float32)),
+                                    _ptr(np.ascontiguousarray(pos, np.int32)), _ptr(kc), _ptr(vc), crs,
+                                    _ptr(np.ascontiguousarray(slots, np.int32)), rows, theta, eps)
+        return qkv, kc, vc
 
     def rmsnorm_gated(self, x, z, w, eps=1e-6):
         dt = dtype_code(x)

@@ -109,6 +109,13 @@ def test_reference_signature_layer(checker, oracle):
     want = oracle.decode_attention(q, kc[None], vc[None], [250], [290])[0].ravel()
     assert np.array_equal(take(np.float32, nq * hd), want)
     assert not np.any(take(np.float32, nq * hd))
+    # kv_ring_advance: the reference's ring (fill, then overwrite the oldest)
+    want = []
+    st_, ln_ = 0, 0
+    for _ in range(7):
+        slot, st_, ln_ = oracle.kv_ring_advance(st_, ln_, 4)
+        want.append(slot)
+    assert list(take(np.int32, 9)) == want + [st_, ln_]
     # a failing call reports through last_status() and the process carries on
     assert take(np.int32, 1)[0] == 1
     assert off == len(raw)

@@ -193,3 +193,60 @@ def test_silu_extremes_f16(ane, oracle):
     want = oracle.silu_mul(g, u)
     assert f16_ulp_diff(out, want).max() <= 1
     assert np.array_equal(np.signbit(out), np.signbit(want))
+
+
+# ------------------------------------------------- KV-cache write after RoPE
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("per_row", [False, True], ids=["prefill", "batched_decode"])
+def test_qk_norm_rope_kv(ane, oracle, dt, per_row):
+    """models/llm/qwen3.cpp:470-488: k after RoPE and v into the ring slot; a
+    row with slot -1 writes no cache row; every other slot keeps its bytes."""
+    torch = _torch()
+    rng = np.random.default_rng(31 + per_row)
+    rows, nq, nkv, hd, cap = 12, 16, 8, 128, 20
+    qkv = rand(rng, (rows, (nq + 2 * nkv) * hd), dt, outliers=0.01)
+    qw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    pos = rng.integers(0, 4096, rows).astype(np.int32)
+    if per_row:
+        shape = (rows, cap, nkv, hd)
+        slots = rng.integers(0, cap, rows).astype(np.int32)
+    else:
+        shape = (cap, nkv, hd)
+        slots = rng.permutation(cap)[:rows].astype(np.int32)  # distinct slots of one ring
+    slots[3] = -1
+    kc = rand(rng, shape, dt)
+    vc = rand(rng, shape, dt)
+    wq, wk, wv = oracle.qk_norm_rope_kv(qkv, nq, nkv, hd, qw, kw, pos, 1e6, kc, vc, slots,
+                                        per_row_cache=per_row)
+    d = to_dev(qkv, dt)
+    dk, dv = to_dev(kc, dt), to_dev(vc, dt)
+    ane.qk_norm_rope_kv(d, torch.from_numpy(qw).cuda(), torch.from_numpy(kw).cuda(),
+                        torch.from_numpy(pos).cuda(), nq, nkv, hd, dk, dv,
+                        torch.from_numpy(slots).cuda())
+    bits = (lambda a: a.view(np.uint32)) if dt == "f32" else (lambda a: a.view(np.uint16))
+    assert np.array_equal(bits(to_host(d, dt)), bits(wq))
+    assert np.array_equal(bits(to_host(dk, dt)), bits(wk))
+    assert np.array_equal(bits(to_host(dv, dt)), bits(wv))
+
+
+def test_qk_norm_rope_kv_bad_slot(ane, oracle):
+    """A slot past the capacity writes no cache row and raises the flag."""
+    torch = _torch()
+    rng = np.random.default_rng(33)
+    rows, nq, nkv, hd, cap = 3, 16, 8, 128, 8
+    qkv = rand(rng, (rows, (nq + 2 * nkv) * hd), "f32")
+    w = np.ones(hd, np.float32)
+    pos = np.zeros(rows, np.int32)
+    slots = np.array([1, cap, 2], np.int32)
+    kc = np.zeros((cap, nkv, hd), np.float32)
+    ok = slots.copy()
+    ok[1] = -1
+    _, wk, wv = oracle.qk_norm_rope_kv(qkv, nq, nkv, hd, w, w, pos, 1e6, kc, kc, ok)
+    ane.read_status_flags(clear=True)
+    dk, dv = torch.zeros(cap, nkv, hd, device="cuda"), torch.zeros(cap, nkv, hd, device="cuda")
+    ane.qk_norm_rope_kv(torch.from_numpy(qkv).cuda(), torch.from_numpy(w).cuda(),
+                        torch.from_numpy(w).cuda(), torch.from_numpy(pos).cuda(), nq, nkv, hd, dk, dv,
+                        torch.from_numpy(slots).cuda())
+    assert ane.read_status_flags(clear=True) & ane.FLAG_BAD_CACHE
+    assert np.array_equal(dk.cpu().numpy(), wk) and np.array_equal(dv.cpu().numpy(), wv)
