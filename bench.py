@@ -311,7 +311,8 @@ def time_e2e_chain(torch, ane, rows, steps, chunks=8):
 def time_extras(torch, ane, reps=20):
     """Secondary configs (per GPU): BF16->FP16 convert of a Qwen3-8B-shaped
     checkpoint (flat), the 256-row sampler, the Qwen3-1.7B prefill chain,
-    the Qwen3-0.6B batch-1 decode chain latency and decode attention."""
+    the Qwen3-0.6B batch-1 decode chain latency, decode attention and the
+    ANE-boundary packing."""
     import ctypes as C
     L = ane.lib()
     out = {}
@@ -405,6 +406,19 @@ def time_extras(torch, ane, reps=20):
                                  "attention_qwen3_8b_b64_l4096_f16": (64, 32, 8, torch.float16)}.items():
         us, gbs = time_attention(torch, ane, B, H, hk, 128, 4096, dt)
         out[name] = {"us": round(us, 2), "gb_s": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
+
+    # fp32 <-> fp16 packing at the ANE boundary: 32,768 tokens x 4096
+    # channels (1,024 surfaces of [4096][32]); 6 bytes per (token, channel)
+    T, Cn = 32768, 4096
+    x = torch.randn(T, Cn, device="cuda", generator=g)
+    surf = torch.zeros((T // 32, Cn, 32), dtype=torch.int16, device="cuda")
+    y = torch.empty_like(x)
+    for name, fn in (("ane_pack_32k_x_4096", lambda: ane.ane_pack(x, surface=surf)),
+                     ("ane_unpack_32k_x_4096", lambda: ane.ane_unpack(surf, T, out=y))):
+        ms = timed(fn, reps)
+        gbs = T * Cn * 6 / ms / 1e6
+        out[name] = {"us": round(ms * 1e3, 2), "gb_s": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4)}
+    del x, surf, y
     return out
 
 
@@ -700,6 +714,15 @@ def run_ncu_case(cases, rows=16384):
                 ane.decode_attention(q, k, v, st, n, max_len=ln)
             torch.cuda.synchronize()
             del q, k, v
+    if "pack" in cases:
+        x = torch.randn(8192, 4096, device="cuda")
+        surf = torch.zeros((256, 4096, 32), dtype=torch.int16, device="cuda")
+        y = torch.empty_like(x)
+        for _ in range(2):
+            ane.ane_pack(x, surface=surf)
+            ane.ane_unpack(surf, 8192, out=y)
+        torch.cuda.synchronize()
+        del x, surf, y
     print("ncu case done:", ",".join(sorted(cases)), flush=True)
 
 
@@ -712,7 +735,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--ncu-case", default="",
-                    help="comma list of chain,convert,sampler,attention: run the small profiling "
+                    help="comma list of chain,convert,sampler,attention,pack: run the small profiling "
                          "case and exit")
     args = ap.parse_args()
     if args.ncu_case:
