@@ -88,11 +88,15 @@ __host__ __device__ constexpr size_t attn_rows_bytes() {  // K rows, and V rows 
     return (AttnShape<T, HD>::VREG ? 1 : 2) * (size_t)kAttnKeys * HD * sizeof(typename T::storage);
 }
 
+// The warp partials of P.V ([warp][G][HD] floats) reuse the K rows, which
+// are dead once the scores are taken: 4 G HD floats <= 64 HD elements.
 template <typename T, int HD, int G>
 __host__ __device__ constexpr size_t attn_smem_bytes() {
+    static_assert((size_t)kAttnWarps * G * HD * sizeof(float) <=
+                      (size_t)kAttnKeys * HD * sizeof(typename T::storage),
+                  "warp partials must fit over the K rows");
     return attn_rows_bytes<T, HD>()
-           + (size_t)kAttnKeys * attn_prow<G>() * sizeof(float)  // P, key-major
-           + (size_t)kAttnWarps * G * HD * sizeof(float);        // warp partials
+           + (size_t)kAttnKeys * attn_prow<G>() * sizeof(float);  // P, key-major
 }
 
 // Dots of one 32-key block (keys kb*32 ..) with GC q heads held in registers.
@@ -166,7 +170,7 @@ decode_attention_kernel(const AttnArgs a) {
     S* const sK = reinterpret_cast<S*>(smem);
     S* const sV = sK + kAttnKeys * HD;  // only when !VREG
     float* const s_p = reinterpret_cast<float*>(smem + attn_rows_bytes<T, HD>());  // [key][PROW]
-    float* const s_red = s_p + kAttnKeys * PROW;                      // [warp][G][HD]
+    float* const s_red = reinterpret_cast<float*>(smem);  // [warp][G][HD], over the K rows
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
     __shared__ int s_last;
@@ -457,6 +461,7 @@ decode_attention_kernel(const AttnArgs a) {
             for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(f[s].y, f[s].x, Lc);
         }
     }
+    __syncthreads();  // the chains are in registers; s_red reuses the (m, l) tile
 #pragma unroll
     for (int it = 0; it < IPT; it++) {
         const int idx = tid + it * kAttnThreads;
