@@ -29,6 +29,8 @@
 // exp is the pinned pinned_expf of ane_common.cuh.
 #pragma once
 
+#include <type_traits>
+
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
@@ -153,6 +155,153 @@ __device__ __forceinline__ void score_block(const typename T::storage* sK,
     }
 #pragma unroll
     for (int g = 0; g < GC; g++) dot[g] = v[0][g];
+}
+
+// The end of a split, shared by the kernels: s_red holds the four warp
+// partials of P.V ([warp][G][HD]), s_m / s_l the split's max and exp-sum as
+// two halves each.  One split: write the output.  Otherwise write the
+// split's (m, l, o) to the workspace; the CTA that finishes last for its
+// (kv head, sequence) merges the splits and writes the output.
+template <typename T, int HD, int G>
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, unsigned char* smem, float* s_red,
+                                            float (&s_m)[G][2], float (&s_l)[G][2], float (&s_M)[G],
+                                            float (&s_L)[G][4], int& s_last, int nsplit, int split,
+                                            int kvh, int64_t b, typename T::storage* out) {
+    using S = typename T::storage;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int h0 = kvh * G;
+    // the split's o = ((R0 + R1) + R2) + R3 over the warps (or, in the
+    // merge, over the four chains)
+    auto sum4 = [&](int g, int d) {
+        const float* r = s_red + g * HD + d;
+        return __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[G * HD]), r[2 * G * HD]), r[3 * G * HD]);
+    };
+
+    if (nsplit == 1) {
+        // the merge below with one split: f = exp(m - m), chains 1-3 empty
+        for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
+            const int g = idx / HD, d = idx % HD;
+            const float m = fmaxf(s_m[g][0], s_m[g][1]);
+            const float f = pinned_expf(__fsub_rn(m, m));
+            const float lsum = __fadd_rn(s_l[g][0], s_l[g][1]);
+            const float L = __fadd_rn(__fadd_rn(__fadd_rn(__fmaf_rn(lsum, f, 0.0f), 0.0f), 0.0f), 0.0f);
+            const float O = __fadd_rn(__fadd_rn(__fadd_rn(__fmaf_rn(sum4(g, d), f, 0.0f), 0.0f), 0.0f), 0.0f);
+            out[idx] = T::from_f(__fmul_rn(O, __fdiv_rn(1.0f, L)));
+        }
+        return;
+    }
+
+    const int64_t pbase = (b * a.n_heads + h0) * (int64_t)a.max_splits;  // (seq, head h0, split 0)
+    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
+        const int g = idx / HD, d = idx % HD;
+        a.part_o[(pbase + (int64_t)g * a.max_splits + split) * HD + d] = sum4(g, d);
+    }
+    if (tid < G) {
+        float* ml = a.part_ml + (pbase + (int64_t)tid * a.max_splits + split) * 2;
+        ml[0] = fmaxf(s_m[tid][0], s_m[tid][1]);
+        ml[1] = __fadd_rn(s_l[tid][0], s_l[tid][1]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(a.counters + b * a.n_kv + kvh, 1u);
+        s_last = prev == (uint32_t)(nsplit - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (tid == 0) a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
+
+    // ---- 3. merge the splits (last CTA of this kv head and sequence) -------
+    // (m_j, l_j) of up to FT splits at a time in shared memory over the K
+    // rows (no longer needed); M = max m_j; f_j = exp(m_j - M) replaces m_j;
+    // O and L as four fmaf chains over j = c4 (mod 4), in order of j.
+    constexpr int FT = (int)((attn_rows_bytes<T, HD>() / sizeof(float2)) / G) & ~3;
+    constexpr int COLS = HD / 4;
+    constexpr int ITEMS = G * 4 * COLS;  // (g, chain, float4 column)
+    constexpr int IPT = (ITEMS + kAttnThreads - 1) / kAttnThreads;
+    float2* const s_ml = reinterpret_cast<float2*>(smem);  // [G][FT]
+    auto load_ml = [&](int s0, int ns) {
+        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
+            const int g = idx / ns, s = s0 + idx % ns;
+            const float2* ml = reinterpret_cast<const float2*>(a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2);
+            s_ml[g * FT + (s - s0)] = __ldcg(ml + s);
+        }
+    };
+    const bool one_tile = nsplit <= FT;
+    if (one_tile) {
+        load_ml(0, nsplit);
+        __syncthreads();
+    }
+    for (int g = w; g < G; g += kAttnWarps) {
+        float mx = -INFINITY;
+        if (one_tile) {
+            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, s_ml[g * FT + s].x);
+        } else {
+            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
+            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, __ldcg(ml + 2 * s));
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        if (lane == 0) s_M[g] = mx;
+    }
+    float4 o[IPT];
+#pragma unroll
+    for (int it = 0; it < IPT; it++) o[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float Lc = 0.0f;
+    for (int s0 = 0; s0 < nsplit; s0 += FT) {
+        const int s1 = min(nsplit, s0 + FT), ns = s1 - s0;
+        __syncthreads();  // s_M ready / the previous tile consumed
+        if (!one_tile) {
+            load_ml(s0, ns);
+            __syncthreads();
+        }
+        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
+            float2& e = s_ml[(idx / ns) * FT + idx % ns];
+            e.x = pinned_expf(__fsub_rn(e.x, s_M[idx / ns]));
+        }
+        __syncthreads();
+#pragma unroll
+        for (int it = 0; it < IPT; it++) {
+            const int idx = tid + it * kAttnThreads;
+            if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
+                const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
+                const float4* po =
+                    reinterpret_cast<const float4*>(a.part_o + (pbase + (int64_t)g * a.max_splits) * HD) + col;
+                const float2* f = s_ml + g * FT - s0;
+#pragma unroll 16
+                for (int s = s0 + c4; s < s1; s += 4) {
+                    const float4 v = __ldcg(po + (int64_t)s * COLS);
+                    const float fs = f[s].x;
+                    o[it].x = __fmaf_rn(v.x, fs, o[it].x);
+                    o[it].y = __fmaf_rn(v.y, fs, o[it].y);
+                    o[it].z = __fmaf_rn(v.z, fs, o[it].z);
+                    o[it].w = __fmaf_rn(v.w, fs, o[it].w);
+                }
+            }
+        }
+        if (tid < 4 * G) {
+            const int c4 = tid & 3, g = tid >> 2;
+            const float2* f = s_ml + g * FT - s0;
+            for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(f[s].y, f[s].x, Lc);
+        }
+    }
+    __syncthreads();  // the chains are in registers; s_red reuses the (m, l) tile
+#pragma unroll
+    for (int it = 0; it < IPT; it++) {
+        const int idx = tid + it * kAttnThreads;
+        if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
+            const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
+            reinterpret_cast<float4*>(s_red + (c4 * G + g) * HD)[col] = o[it];
+        }
+    }
+    if (tid < 4 * G) s_L[tid >> 2][tid & 3] = Lc;
+    __syncthreads();
+    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
+        const int g = idx / HD, d = idx % HD;
+        const float L = __fadd_rn(__fadd_rn(__fadd_rn(s_L[g][0], s_L[g][1]), s_L[g][2]), s_L[g][3]);
+        out[idx] = T::from_f(__fmul_rn(sum4(g, d), __fdiv_rn(1.0f, L)));
+    }
 }
 
 template <typename T, int HD, int G>
@@ -345,140 +494,255 @@ decode_attention_kernel(const AttnArgs a) {
     }
     __syncthreads();
 
-    // the split's o = ((R0 + R1) + R2) + R3 over the warps (or, in the
-    // merge, over the four chains)
-    auto sum4 = [&](int g, int d) {
-        const float* r = s_red + g * HD + d;
-        return __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[G * HD]), r[2 * G * HD]), r[3 * G * HD]);
-    };
+    attn_finish<T, HD, G>(a, smem, s_red, s_m, s_l, s_M, s_L, s_last, nsplit, split, kvh, b, out);
+}
 
-    if (nsplit == 1) {
-        // the merge below with one split: f = exp(m - m), chains 1-3 empty
-        for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
-            const int g = idx / HD, d = idx % HD;
-            const float m = fmaxf(s_m[g][0], s_m[g][1]);
-            const float f = pinned_expf(__fsub_rn(m, m));
-            const float lsum = __fadd_rn(s_l[g][0], s_l[g][1]);
-            const float L = __fadd_rn(__fadd_rn(__fadd_rn(__fmaf_rn(lsum, f, 0.0f), 0.0f), 0.0f), 0.0f);
-            const float O = __fadd_rn(__fadd_rn(__fadd_rn(__fmaf_rn(sum4(g, d), f, 0.0f), 0.0f), 0.0f), 0.0f);
-            out[idx] = T::from_f(__fmul_rn(O, __fdiv_rn(1.0f, L)));
+
+// ---------------------------------------------------------------------------
+// 16-bit caches: the same split structure with the two contractions on the
+// tensor cores (mma.sync m16n8k16, fp32 accumulation).  Rows of the MMA are
+// the kv head's q heads (G <= 8 of 16; the rest are zero), so one warp's
+// scores for its 16 keys are two MMA tiles per 16 dims, and P.V for those
+// keys is one 16-deep k-step per 8 dims.  The exps stay in registers and are
+// the A operand of P.V directly (the accumulator layout of the first MMA is
+// the operand layout of the second).  P is split into a high and a low part
+// in the cache's type (fp16 scaled by 2^12 so the low part stays normal), so
+// P.V keeps about 16 (bf16) / 22 (fp16) significant bits of each weight.
+// The MMA's internal summation order is the hardware's: results agree with
+// the fp32 CUDA-core order to within the output type's rounding (one unit).
+// K and V rows sit in shared memory with a 16-byte pad per row, which makes
+// the fragment loads (32-bit loads for K, ldmatrix.trans for V) free of bank
+// conflicts.
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+                                         uint32_t b1) {
+    const uint32_t z = 0u;  // rows 8-15 of A: no heads there
+    if constexpr (std::is_same<T, F16>::value)
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
+                     "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                     : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+    else
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
+                     "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                     : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                     : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+// two floats -> a packed pair of T (element 0 in the low half)
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float x0, float x1) {
+    if constexpr (std::is_same<T, F16>::value) {
+        const __half2 h = __floats2half2_rn(x0, x1);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+        return *reinterpret_cast<const uint32_t*>(&h);
+    }
+}
+template <typename T>
+__device__ __forceinline__ float low_f(uint32_t v) {  // element 0 of a packed pair
+    return T::to_f(*reinterpret_cast<const typename T::storage*>(&v));
+}
+template <typename T>
+__device__ __forceinline__ float high_f(uint32_t v) {
+    const uint32_t hi = v >> 16;
+    return T::to_f(*reinterpret_cast<const typename T::storage*>(&hi));
+}
+
+template <int HD>
+__host__ __device__ constexpr int attn_mma_rs() { return HD + 8; }  // padded row, elements
+
+template <int HD>
+__host__ __device__ constexpr size_t attn_mma_smem_bytes() {
+    return 2 * (size_t)kAttnKeys * attn_mma_rs<HD>() * 2;  // K and V rows, 16-bit
+}
+
+template <typename T, int HD, int G>
+__global__ void __launch_bounds__(kAttnThreads)
+decode_attention_mma_kernel(const AttnArgs a) {
+    using S = typename T::storage;
+    static_assert(sizeof(S) == 2, "16-bit caches");
+    static_assert(G <= 8, "at most 8 q heads per kv head");
+    constexpr int RS = attn_mma_rs<HD>();
+    constexpr uint32_t ROW = HD * sizeof(S);
+    constexpr int KSTEPS = HD / 16;
+    constexpr bool F16S = std::is_same<T, F16>::value;
+    constexpr float PSCALE = F16S ? 4096.0f : 1.0f;  // 2^12: fp16 low parts stay normal
+    static_assert((size_t)kAttnWarps * G * HD * sizeof(float) <= (size_t)kAttnKeys * RS * sizeof(S),
+                  "warp partials must fit over the K rows");
+    static_assert(attn_rows_bytes<T, HD>() <= attn_mma_smem_bytes<HD>(), "merge tile");
+    extern __shared__ __align__(16) unsigned char smem[];
+    S* const sK = reinterpret_cast<S*>(smem);
+    S* const sV = sK + kAttnKeys * RS;
+    float* const s_red = reinterpret_cast<float*>(smem);  // [warp][G][HD], over the K rows
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
+    __shared__ float s_wm[G][kAttnWarps], s_wl[G][kAttnWarps];
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int gid = lane >> 2, tq = lane & 3;  // MMA fragment row / column pair
+    const int split = blockIdx.x, kvh = blockIdx.y;
+    const int64_t b = blockIdx.z;
+    const int len = __ldg(a.len + b), start = __ldg(a.start + b);
+    const int h0 = kvh * G;
+    S* const out = static_cast<S*>(a.out) + b * a.out_stride + (int64_t)h0 * HD;
+
+    const bool bad = len > a.capacity || len > a.max_len ||
+                     (len > 0 && (start < 0 || start >= a.capacity));
+    if (len <= 0 || bad) {  // core/cpu_ops.cpp:176-179: no keys -> zeros
+        if (split == 0) {
+            for (int i = tid; i < G * HD; i += kAttnThreads) out[i] = T::from_f(0.0f);
+            if (bad && tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_BAD_CACHE);
         }
         return;
     }
+    const int nsplit = (len + kAttnKeys - 1) / kAttnKeys;
+    if (split >= nsplit) return;
+    const int t0 = split * kAttnKeys;
+    const int n = min(kAttnKeys, len - t0);
 
-    const int64_t pbase = (b * a.n_heads + h0) * (int64_t)a.max_splits;  // (seq, head h0, split 0)
-    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
-        const int g = idx / HD, d = idx % HD;
-        a.part_o[(pbase + (int64_t)g * a.max_splits + split) * HD + d] = sum4(g, d);
+    // ---- 1. stage K and V rows (padded) ------------------------------------
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
     }
-    if (tid < G) {
-        float* ml = a.part_ml + (pbase + (int64_t)tid * a.max_splits + split) * 2;
-        ml[0] = fmaxf(s_m[tid][0], s_m[tid][1]);
-        ml[1] = __fadd_rn(s_l[tid][0], s_l[tid][1]);
-    }
-    __threadfence();
     __syncthreads();
     if (tid == 0) {
-        const uint32_t prev = atomicAdd(a.counters + b * a.n_kv + kvh, 1u);
-        s_last = prev == (uint32_t)(nsplit - 1);
+        mbar_expect_tx(&bars[0], (uint32_t)n * ROW);
+        mbar_expect_tx(&bars[1], (uint32_t)n * ROW);
     }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    if (tid == 0) a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
+    __syncthreads();  // byte counts registered before any copy is issued
+    {
+        const int i = tid & (kAttnKeys - 1);  // threads 0-63 copy K rows, 64-127 V rows
+        if (i < n) {
+            int slot = start + t0 + i;  // ring position (models/llm/qwen3.cpp:190-204)
+            if (slot >= a.capacity) slot -= a.capacity;
+            const int64_t off = b * a.cache_stride + ((int64_t)slot * a.n_kv + kvh) * HD;
+            if (tid < kAttnKeys)
+                bulk_load(sK + i * RS, static_cast<const S*>(a.k_cache) + off, ROW, &bars[0]);
+            else
+                bulk_load(sV + i * RS, static_cast<const S*>(a.v_cache) + off, ROW, &bars[1]);
+        } else if (tid >= kAttnKeys) {
+            // V rows past the keys enter P.V with weight 0: make them finite
+            uint4* z = reinterpret_cast<uint4*>(sV + i * RS);
+            for (int c = 0; c < (int)(ROW / 16); c++) z[c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
 
-    // ---- 3. merge the splits (last CTA of this kv head and sequence) -------
-    // (m_j, l_j) of up to FT splits at a time in shared memory over the K
-    // rows (no longer needed); M = max m_j; f_j = exp(m_j - M) replaces m_j;
-    // O and L as four fmaf chains over j = c4 (mod 4), in order of j.
-    constexpr int FT = (int)((attn_rows_bytes<T, HD>() / sizeof(float2)) / G) & ~3;
-    constexpr int COLS = HD / 4;
-    constexpr int ITEMS = G * 4 * COLS;  // (g, chain, float4 column)
-    constexpr int IPT = (ITEMS + kAttnThreads - 1) / kAttnThreads;
-    float2* const s_ml = reinterpret_cast<float2*>(smem);  // [G][FT]
-    auto load_ml = [&](int s0, int ns) {
-        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
-            const int g = idx / ns, s = s0 + idx % ns;
-            const float2* ml = reinterpret_cast<const float2*>(a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2);
-            s_ml[g * FT + (s - s0)] = __ldcg(ml + s);
-        }
-    };
-    const bool one_tile = nsplit <= FT;
-    if (one_tile) {
-        load_ml(0, nsplit);
-        __syncthreads();
-    }
-    for (int g = w; g < G; g += kAttnWarps) {
-        float mx = -INFINITY;
-        if (one_tile) {
-            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, s_ml[g * FT + s].x);
-        } else {
-            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
-            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, __ldcg(ml + 2 * s));
-        }
+    // q fragments (rows = heads gid < G; others zero), loaded while the copies fly
+    uint32_t qa[KSTEPS][2];
+    {
+        const bool hv = gid < G;
+        const S* qp = static_cast<const S*>(a.q) + b * a.q_stride +
+                      (int64_t)(h0 + (hv ? gid : 0)) * a.q_head_stride + 2 * tq;
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-        if (lane == 0) s_M[g] = mx;
-    }
-    float4 o[IPT];
-#pragma unroll
-    for (int it = 0; it < IPT; it++) o[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    float Lc = 0.0f;
-    for (int s0 = 0; s0 < nsplit; s0 += FT) {
-        const int s1 = min(nsplit, s0 + FT), ns = s1 - s0;
-        __syncthreads();  // s_M ready / the previous tile consumed
-        if (!one_tile) {
-            load_ml(s0, ns);
-            __syncthreads();
-        }
-        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
-            float2& e = s_ml[(idx / ns) * FT + idx % ns];
-            e.x = pinned_expf(__fsub_rn(e.x, s_M[idx / ns]));
-        }
-        __syncthreads();
-#pragma unroll
-        for (int it = 0; it < IPT; it++) {
-            const int idx = tid + it * kAttnThreads;
-            if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
-                const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
-                const float4* po =
-                    reinterpret_cast<const float4*>(a.part_o + (pbase + (int64_t)g * a.max_splits) * HD) + col;
-                const float2* f = s_ml + g * FT - s0;
-#pragma unroll 16
-                for (int s = s0 + c4; s < s1; s += 4) {
-                    const float4 v = __ldcg(po + (int64_t)s * COLS);
-                    const float fs = f[s].x;
-                    o[it].x = __fmaf_rn(v.x, fs, o[it].x);
-                    o[it].y = __fmaf_rn(v.y, fs, o[it].y);
-                    o[it].z = __fmaf_rn(v.z, fs, o[it].z);
-                    o[it].w = __fmaf_rn(v.w, fs, o[it].w);
-                }
-            }
-        }
-        if (tid < 4 * G) {
-            const int c4 = tid & 3, g = tid >> 2;
-            const float2* f = s_ml + g * FT - s0;
-            for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(f[s].y, f[s].x, Lc);
+        for (int ks = 0; ks < KSTEPS; ks++) {
+            qa[ks][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qp + 16 * ks)) : 0u;
+            qa[ks][1] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qp + 16 * ks + 8)) : 0u;
         }
     }
-    __syncthreads();  // the chains are in registers; s_red reuses the (m, l) tile
+
+    if (!__syncthreads_and(mbar_wait_bounded(&bars[0], 0))) {
+        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+        return;
+    }
+
+    // ---- 2a. scores: warp w takes keys 16w .. 16w+15 (two 8-key tiles) ----
+    float sc[2][4];
 #pragma unroll
-    for (int it = 0; it < IPT; it++) {
-        const int idx = tid + it * kAttnThreads;
-        if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
-            const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
-            reinterpret_cast<float4*>(s_red + (c4 * G + g) * HD)[col] = o[it];
+    for (int nb = 0; nb < 2; nb++) {
+        sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
+        const S* kr = sK + (16 * w + 8 * nb + gid) * RS + 2 * tq;
+#pragma unroll
+        for (int ks = 0; ks < KSTEPS; ks++) {
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks + 8);
+            mma16816<T>(sc[nb], qa[ks][0], qa[ks][1], b0, b1);
         }
     }
-    if (tid < 4 * G) s_L[tid >> 2][tid & 3] = Lc;
+    // this thread: head gid, keys 16w + 2tq + {0, 1, 8, 9}
+    const int kbase = 16 * w + 2 * tq;
+    float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+    const int koff[4] = {0, 1, 8, 9};
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        x[i] = kbase + koff[i] < n ? __fmul_rn(x[i], a.scale) : -INFINITY;
+        mx = fmaxf(mx, x[i]);
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (tq == 0 && gid < G) s_wm[gid][w] = mx;
     __syncthreads();
-    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
-        const int g = idx / HD, d = idx % HD;
-        const float L = __fadd_rn(__fadd_rn(__fadd_rn(s_L[g][0], s_L[g][1]), s_L[g][2]), s_L[g][3]);
-        out[idx] = T::from_f(__fmul_rn(sum4(g, d), __fdiv_rn(1.0f, L)));
+    float e[4], es = 0.0f;
+    {
+        const int g = gid < G ? gid : 0;
+        const float m = fmaxf(fmaxf(s_wm[g][0], s_wm[g][1]), fmaxf(s_wm[g][2], s_wm[g][3]));
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            e[i] = (gid < G && kbase + koff[i] < n) ? pinned_expf(__fsub_rn(x[i], m)) : 0.0f;
+            es = __fadd_rn(es, e[i]);
+        }
     }
+    es = __fadd_rn(es, __shfl_xor_sync(0xffffffffu, es, 1));
+    es = __fadd_rn(es, __shfl_xor_sync(0xffffffffu, es, 2));
+    if (tq == 0 && gid < G) s_wl[gid][w] = es;
+    // P as the A operand of P.V: high and low parts
+    uint32_t ph[2], pl[2];
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        const float p0 = __fmul_rn(e[2 * j], PSCALE), p1 = __fmul_rn(e[2 * j + 1], PSCALE);
+        ph[j] = pack2<T>(p0, p1);
+        pl[j] = pack2<T>(__fsub_rn(p0, low_f<T>(ph[j])), __fsub_rn(p1, high_f<T>(ph[j])));
+    }
+    if (!__syncthreads_and(mbar_wait_bounded(&bars[1], 0))) {
+        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+        return;
+    }
+
+    // ---- 2b. P.V over the warp's 16 keys ------------------------------------
+    float o[HD / 8][4];
+#pragma unroll
+    for (int nb = 0; nb < HD / 8; nb++) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
+    {
+        const int mi = lane >> 3, rr = lane & 7;
+        const S* vb = sV + (16 * w + (mi & 1) * 8 + rr) * RS + (mi >> 1) * 8;
+#pragma unroll
+        for (int d0 = 0; d0 < HD; d0 += 16) {
+            uint32_t r[4];
+            ldsm_x4_trans(r, vb + d0);
+            mma16816<T>(o[d0 / 8], ph[0], ph[1], r[0], r[1]);
+            mma16816<T>(o[d0 / 8], pl[0], pl[1], r[0], r[1]);
+            mma16816<T>(o[d0 / 8 + 1], ph[0], ph[1], r[2], r[3]);
+            mma16816<T>(o[d0 / 8 + 1], pl[0], pl[1], r[2], r[3]);
+        }
+    }
+    __syncthreads();  // every warp is done with the K rows before s_red overwrites them
+    if (gid < G) {
+        constexpr float UNSCALE = 1.0f / PSCALE;
+#pragma unroll
+        for (int nb = 0; nb < HD / 8; nb++)
+            *reinterpret_cast<float2*>(s_red + (w * G + gid) * HD + 8 * nb + 2 * tq) =
+                make_float2(__fmul_rn(o[nb][0], UNSCALE), __fmul_rn(o[nb][1], UNSCALE));
+    }
+    if (tid < G) {
+        s_m[tid][0] = fmaxf(s_wm[tid][0], s_wm[tid][1]);
+        s_m[tid][1] = fmaxf(s_wm[tid][2], s_wm[tid][3]);
+        s_l[tid][0] = __fadd_rn(s_wl[tid][0], s_wl[tid][1]);
+        s_l[tid][1] = __fadd_rn(s_wl[tid][2], s_wl[tid][3]);
+    }
+    __syncthreads();
+    attn_finish<T, HD, G>(a, smem, s_red, s_m, s_l, s_M, s_L, s_last, nsplit, split, kvh, b, out);
 }
-
 
 // Launches the kernel instance for (head_dim, group); ANE_CUDA_ERR_UNSUPPORTED
 // for shapes without one.
@@ -492,8 +756,16 @@ namespace ane {
 
 template <typename T, int HD, int G>
 int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
-    constexpr size_t smem = attn_smem_bytes<T, HD, G>();
-    auto kern = decode_attention_kernel<T, HD, G>;
+    // 16-bit caches: the tensor-core kernel; fp32: the CUDA-core kernel
+    size_t smem;
+    void (*kern)(AttnArgs);
+    if constexpr (sizeof(typename T::storage) == 2) {
+        smem = attn_mma_smem_bytes<HD>();
+        kern = decode_attention_mma_kernel<T, HD, G>;
+    } else {
+        smem = attn_smem_bytes<T, HD, G>();
+        kern = decode_attention_kernel<T, HD, G>;
+    }
     if (smem > 48 * 1024) {
         const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess)
