@@ -55,6 +55,25 @@ def env_rank():
             int(os.environ.get("WORLD_SIZE", "1")))
 
 
+def rank_rows(rank, rows_per_rank=None):
+    """Weak scaling: rank r owns global rows [r * R, (r + 1) * R) of the
+    batched-prefill chain (R = ROWS).  Rows are independent, so a rank's
+    inputs come from the seed and its row offset and nothing crosses ranks
+    on the data path."""
+    r = ROWS if rows_per_rank is None else rows_per_rank
+    return rank * r, r
+
+
+def chain_seed(row0):
+    """Seed of a rank's synthetic inputs: the base seed plus its row offset."""
+    return 1234 + row0
+
+
+def aggregate_gbs(world, rows_per_rank, ms):
+    """Whole-job GB/s of the chain: every rank's rows over the slowest rank's time."""
+    return world * rows_per_rank * B_ROW / (ms * 1e-3) / 1e9
+
+
 def host_threads():
     try:
         return len(os.sched_getaffinity(0))
@@ -229,9 +248,12 @@ def time_device_chain(torch, dist, world, chain, steps, warmup, gpu_index):
 
 
 def max_over_ranks(torch, dist, world, v):
+    """The slowest rank's value: a one-element MAX all-reduce (the timing
+    collective, never on the data path); on the CPU backend (gloo) too."""
     if world == 1:
         return v
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
 
@@ -609,13 +631,14 @@ def run_ours(args):
     rank, local, world = env_rank()
     torch, ane, rank, local = _setup_gpu(world)
     cur = torch.cuda.current_stream()
-    b = make_chain_inputs(torch, ROWS, HIDDEN, NQ, NKV, HD, INTER, SEQ, 1234 + rank)
+    row0, nrows = rank_rows(rank)
+    b = make_chain_inputs(torch, nrows, HIDDEN, NQ, NKV, HD, INTER, SEQ, chain_seed(row0))
     chain = Chain(ane, b, ROWS, HIDDEN, NQ, NKV, HD, INTER, cur.cuda_stream)
     total_ms, per, clocks = time_device_chain(torch, dist, world, chain, args.steps,
                                               args.warmup, local)
     total_ms = max_over_ranks(torch, dist, world, total_ms)
     ms_step = total_ms / args.steps
-    value = world * ROWS * B_ROW / (ms_step * 1e-3) / 1e9
+    value = aggregate_gbs(world, nrows, ms_step)
     peak, peak_kind = measured_peak()
     names = ["residual_rmsnorm", "qk_norm_rope", "silu_mul"]
     bytes_k = [ROWS * B_NORM, ROWS * B_QK, ROWS * B_SILU]
@@ -634,7 +657,7 @@ def run_ours(args):
         dist.barrier()
     e_ms, h2d, d2h, e_launches = time_e2e_chain(torch, ane, ROWS, e2e_steps)
     e_ms = max_over_ranks(torch, dist, world, e_ms)
-    e2e_val = world * ROWS * B_ROW / (e_ms * 1e-3) / 1e9
+    e2e_val = aggregate_gbs(world, nrows, e_ms)
     torch.cuda.empty_cache()
 
     extras = time_extras(torch, ane) if (rank == 0 and not args.no_extras) else None
