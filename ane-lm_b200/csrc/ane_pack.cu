@@ -10,10 +10,12 @@
 // leaves slots 1-31.
 //
 // Both directions are transposes: one CTA takes one surface (32 tokens) and
-// a chunk of kPackCh channels, stages the fp32 tile in shared memory (rows
-// padded to stride kPackCh + 1, so both access patterns are conflict-free),
-// and moves rows of the other layout with 16-byte accesses: token rows of
-// kPackCh floats, surface rows of 32 halves (64 bytes).
+// a chunk of kPackCh channels, stages the fp32 tile in shared memory and
+// moves rows of the other layout with 16-byte accesses: token rows of
+// kPackCh floats, surface rows of 32 halves (64 bytes).  The tile keeps
+// 16-byte aligned token rows and swizzles their 4-channel chunks by the
+// token's group of 8 (chunk ^ (t / 8) % 8), so that the float4 row accesses
+// and the per-channel column accesses are both free of bank conflicts.
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
@@ -22,7 +24,11 @@ namespace ane {
 constexpr int kSpatial = 32;
 constexpr int kPackCh = 128;      // channels per CTA
 constexpr int kPackThreads = 256;
-constexpr int kPackStride = kPackCh + 1;
+
+// tile slot of (token t, channel c)
+__device__ __forceinline__ int tslot(int t, int c) {
+    return t * kPackCh + ((((c >> 2) ^ ((t >> 3) & 7))) << 2) + (c & 3);
+}
 
 // f32 -> f16 bits.  Round to nearest even as the arm64 __fp16 store does
 // (core/ane_runtime.cpp:624), NaN -> quiet NaN 0x7E00 with the sign.
@@ -46,7 +52,16 @@ __device__ __forceinline__ uint16_t f2h_trunc(float x) {
     return sign | ((uint32_t)e << 10) | (frac >> 13);
 }
 
-// f16 bits -> f32, exact, NaN payloads kept (include/ane_lm/common.h:35-56).
+// f16 bits -> f32, exact, NaN payloads kept (include/ane_lm/common.h:35-56):
+// the hardware conversion is exact for every non-NaN half; a NaN is rebuilt
+// with its payload.
+__device__ __forceinline__ float h2f_fast(uint32_t h) {
+    const float f = __half2float(__ushort_as_half((unsigned short)h));
+    const bool nan = (h & 0x7C00u) == 0x7C00u && (h & 0x3FFu) != 0u;
+    return nan ? __uint_as_float(((h & 0x8000u) << 16) | 0x7F800000u | ((h & 0x3FFu) << 13)) : f;
+}
+
+// The same by integer operations (the generic path).
 __device__ __forceinline__ float h2f_exact(uint32_t h) {
     const uint32_t sign = (h & 0x8000u) << 16;
     const uint32_t e = (h >> 10) & 0x1Fu, m = h & 0x3FFu;
@@ -69,7 +84,7 @@ template <bool TRUNC, bool VEC>
 __global__ void __launch_bounds__(kPackThreads)
 ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, int64_t in_stride,
                 int64_t tokens, int channels) {
-    __shared__ float tile[kSpatial * kPackStride];
+    __shared__ __align__(16) float tile[kSpatial * kPackCh];
     const int64_t s = blockIdx.x;
     const int c0 = blockIdx.y * kPackCh;
     const int nc = min(kPackCh, channels - c0);
@@ -79,15 +94,11 @@ ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, in
     // token rows -> tile[t][c]
     for (int r = w; r < nt; r += kPackThreads / kWarp) {
         const float* row = in + (t0 + r) * in_stride + c0;
-        float* trow = tile + r * kPackStride;
         if (VEC && nc == kPackCh) {
             const float4 v = __ldcs(reinterpret_cast<const float4*>(row) + lane);
-            trow[4 * lane] = v.x;
-            trow[4 * lane + 1] = v.y;
-            trow[4 * lane + 2] = v.z;
-            trow[4 * lane + 3] = v.w;
+            *reinterpret_cast<float4*>(tile + tslot(r, 4 * lane)) = v;
         } else {
-            for (int c = lane; c < nc; c += kWarp) trow[c] = __ldcs(row + c);
+            for (int c = lane; c < nc; c += kWarp) tile[tslot(r, c)] = __ldcs(row + c);
         }
     }
     __syncthreads();
@@ -96,10 +107,11 @@ ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, in
     for (int item = tid; item < nc * 4; item += kPackThreads) {
         const int c = item >> 2, q = item & 3;
         uint16_t* dst = sbase + c * kSpatial + 8 * q;
+        const float* col = tile + tslot(8 * q, c);  // tokens 8q .. 8q+7 share the swizzle
         if (nt == kSpatial) {
             uint32_t h[8];
 #pragma unroll
-            for (int i = 0; i < 8; i++) h[i] = f2h<TRUNC>(tile[(8 * q + i) * kPackStride + c]);
+            for (int i = 0; i < 8; i++) h[i] = f2h<TRUNC>(col[i * kPackCh]);
             uint4 v;
             v.x = h[0] | (h[1] << 16);
             v.y = h[2] | (h[3] << 16);
@@ -108,7 +120,7 @@ ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, in
             __stcs(reinterpret_cast<uint4*>(dst), v);
         } else {
             for (int i = 0; i < 8 && 8 * q + i < nt; i++)
-                dst[i] = (uint16_t)f2h<TRUNC>(tile[(8 * q + i) * kPackStride + c]);
+                dst[i] = (uint16_t)f2h<TRUNC>(col[i * kPackCh]);
         }
     }
 }
@@ -118,7 +130,7 @@ template <bool VEC>
 __global__ void __launch_bounds__(kPackThreads)
 ane_unpack_kernel(float* __restrict__ out, int64_t out_stride, const uint16_t* __restrict__ surface,
                   int64_t tokens, int channels) {
-    __shared__ float tile[kSpatial * kPackStride];
+    __shared__ __align__(16) float tile[kSpatial * kPackCh];
     const int64_t s = blockIdx.x;
     const int c0 = blockIdx.y * kPackCh;
     const int nc = min(kPackCh, channels - c0);
@@ -131,19 +143,18 @@ ane_unpack_kernel(float* __restrict__ out, int64_t out_stride, const uint16_t* _
         if (8 * q >= nt) continue;
         const uint4 v = __ldcs(reinterpret_cast<const uint4*>(sbase + c * kSpatial + 8 * q));
         const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+        float* col = tile + tslot(8 * q, c);  // tokens 8q .. 8q+7 share the swizzle
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-            tile[(8 * q + i) * kPackStride + c] = h2f_exact((wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
+        for (int i = 0; i < 8; i++) col[i * kPackCh] = h2f_fast((wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
     }
     __syncthreads();
     for (int r = w; r < nt; r += kPackThreads / kWarp) {
         float* row = out + (t0 + r) * out_stride + c0;
-        const float* trow = tile + r * kPackStride;
         if (VEC && nc == kPackCh) {
             __stcs(reinterpret_cast<float4*>(row) + lane,
-                   make_float4(trow[4 * lane], trow[4 * lane + 1], trow[4 * lane + 2], trow[4 * lane + 3]));
+                   *reinterpret_cast<const float4*>(tile + tslot(r, 4 * lane)));
         } else {
-            for (int c = lane; c < nc; c += kWarp) __stcs(row + c, trow[c]);
+            for (int c = lane; c < nc; c += kWarp) __stcs(row + c, tile[tslot(r, c)]);
         }
     }
 }
