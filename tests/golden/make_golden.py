@@ -148,6 +148,70 @@ def main():
         np.savez_compressed(os.path.join(HERE, "convert_blobs.npz"),
                             safetensors=np.frombuffer(open(path, "rb").read(), np.uint8),
                             **{"blob:" + k: v for k, v in files.items()})
+    # Fixtures of the next rows, from their own random stream so the ones
+    # above stay as they were.
+    rng2 = np.random.default_rng(4321)
+
+    # 7. gqa_attention (core/cpu_ops.cpp:173-240) over rings, fp32 (inputs on
+    #    a 1/64 grid, exact in fp16, stored as fp16 so the fixture stays
+    #    small; the arithmetic is full fp32)
+    att = {}
+    q64 = lambda shape: (np.round(rng2.standard_normal(shape) * 64) / 64).astype(np.float32)  # noqa: E731
+    for i, (H, hk, hd, cap, start, ln) in enumerate([(8, 2, 128, 256, 250, 256),
+                                                     (32, 8, 128, 70, 60, 69),
+                                                     (16, 4, 128, 200, 150, 190),
+                                                     (16, 8, 128, 64, 7, 1),
+                                                     (8, 8, 64, 100, 99, 37)]):
+        q, k, v = q64((H, hd)), q64((cap, hk, hd)), q64((cap, hk, hd))
+        o = np.empty((H, hd), np.float32)
+        ref.ref_gqa_attention(ptr(o), ptr(q), ptr(k), ptr(v), H, hk, hd, hd, start, ln, cap)
+        att.update({f"q{i}": q.astype(np.float16), f"k{i}": k.astype(np.float16),
+                    f"v{i}": v.astype(np.float16), f"out{i}": o,
+                    f"ring{i}": np.array([start, ln, cap], np.int32)})
+    np.savez_compressed(os.path.join(HERE, "gqa_attention.npz"), **att)
+
+    # 8. rmsnorm_gated (:33-39) and l2_normalize (:106-111), fp32 rows of 128
+    x = (rng2.standard_normal((16, 128)) * 2).astype(np.float32)
+    z = (rng2.standard_normal((16, 128)) * 4).astype(np.float32)
+    z[0, :3] = [-90.0, 90.0, 40.0]
+    w = (1.0 + 0.1 * rng2.standard_normal(128)).astype(np.float32)
+    gated = np.empty_like(x)
+    l2 = x.copy()
+    for r in range(x.shape[0]):
+        ref.ref_rmsnorm_gated(ptr(gated[r]), ptr(x[r]), ptr(z[r]), ptr(w), 128)
+        ref.ref_l2_normalize(ptr(l2[r]), 128)
+    np.savez_compressed(os.path.join(HERE, "hybrid_rows.npz"), x=x, z=z, w=w, gated=gated, l2=l2)
+
+    # 9. the ANE-boundary conversions of the x86 branch (common.h:35-71):
+    #    f32 -> f16 by truncation over random bit patterns and specials,
+    #    f16 -> f32 over every half
+    f32 = rng2.integers(0, 1 << 32, 8192, dtype=np.uint64).astype(np.uint32)
+    f32[:8] = [0x7F800000, 0xFF800000, 0x7FC00000, 0x33000001, 0x387FC000, 0x477FF000, 0x1, 0x3F801000]
+    f32 = f32.view(np.float32)
+    trunc = np.empty(f32.size, np.uint16)
+    ref.ref_f32_to_f16_vec(ptr(trunc), ptr(f32), f32.size)
+    h = np.arange(65536, dtype=np.uint16)
+    widen = np.empty(h.size, np.float32)
+    ref.ref_f16_to_f32_vec(ptr(widen), ptr(h), h.size)
+    np.savez_compressed(os.path.join(HERE, "ane_convert.npz"), f32=f32, trunc=trunc, widen=widen)
+
+    # 10. load_bf16_to_f32 and the (1 + w) load_norm_weight (safetensors.cpp:264-306)
+    b = rng2.integers(0, 65536, 2048, dtype=np.uint64).astype(np.uint16)
+    b[:5] = [0x7F80, 0xFF80, 0x7FC1, 0x8000, 0x3F80]
+    with tempfile.TemporaryDirectory() as td:
+        import json
+        js = json.dumps({"model.norm.weight": {"dtype": "BF16", "shape": [2048],
+                                               "data_offsets": [0, 4096]}})
+        path = os.path.join(td, "w.safetensors")
+        with open(path, "wb") as fh:
+            fh.write(struct.pack("<Q", len(js)))
+            fh.write(js.encode())
+            fh.write(b.tobytes())
+        plain = np.empty(2048, np.float32)
+        norm = np.empty(2048, np.float32)
+        assert ref.ref_load_weight(path.encode(), b"model.norm.weight", 2048, 0, ptr(plain)) == 0
+        assert ref.ref_load_weight(path.encode(), b"model.norm.weight", 2048, 1, ptr(norm)) == 0
+    np.savez_compressed(os.path.join(HERE, "norm_weight.npz"), bf16=b, plain=plain, norm=norm)
     print("golden fixtures written to", HERE)
 
 

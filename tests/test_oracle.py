@@ -349,3 +349,42 @@ def test_norm_weight_load_vs_reference(oracle, ref, tmp_path):
         assert ref.ref_load_weight(path.encode(), b"model.norm.weight", 4096, norm, ptr(want)) == 0
         got = oracle.bf16_to_f32_weights(b, norm)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), norm
+
+
+# ------------------------------------------- golden fixtures of the next rows
+def test_gqa_attention_golden(oracle):
+    """The oracle's attention within 1e-6 x max|v| of the reference's outputs
+    in tests/golden/gqa_attention.npz (different, fixed summation orders)."""
+    g = np.load(os.path.join(GOLDEN, "gqa_attention.npz"))
+    i = 0
+    while f"q{i}" in g:
+        q, k, v = (g[f"{n}{i}"].astype(np.float32) for n in "qkv")
+        start, ln, cap = (int(t) for t in g[f"ring{i}"])
+        got = oracle.decode_attention(q[None], k[None], v[None], [start], [ln])[0]
+        assert np.abs(got - g[f"out{i}"]).max() <= 1e-6 * np.abs(v).max(), i
+        i += 1
+    assert i == 5
+
+
+def test_hybrid_rows_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "hybrid_rows.npz"))
+    gated = oracle.rmsnorm_gated(g["x"], g["z"], g["w"])
+    assert np.array_equal(gated.view(np.uint32), g["gated"].view(np.uint32))
+    l2 = oracle.l2_normalize(g["x"])
+    assert np.array_equal(l2.view(np.uint32), g["l2"].view(np.uint32))
+
+
+def test_ane_convert_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "ane_convert.npz"))
+    got = oracle.ane_pack(g["f32"].reshape(1, -1), round_mode=1, spatial=1).ravel()
+    assert np.array_equal(got, g["trunc"])
+    h = np.arange(65536, dtype=np.uint16)
+    w = oracle.ane_unpack(h.reshape(1, -1, 1), tokens=1, spatial=1).ravel()
+    assert np.array_equal(w.view(np.uint32), g["widen"].view(np.uint32))
+
+
+def test_norm_weight_golden(oracle):
+    g = np.load(os.path.join(GOLDEN, "norm_weight.npz"))
+    for key, add in (("plain", False), ("norm", True)):
+        got = oracle.bf16_to_f32_weights(g["bf16"], add)
+        assert np.array_equal(got.view(np.uint32), g[key].view(np.uint32)), key
