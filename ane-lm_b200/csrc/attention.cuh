@@ -201,16 +201,22 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, unsigned char* sm
         ml[0] = fmaxf(s_m[tid][0], s_m[tid][1]);
         ml[1] = __fadd_rn(s_l[tid][0], s_l[tid][1]);
     }
-    __threadfence();
+    // Release the partials with one fence after the CTA barrier (the barrier
+    // orders every thread's stores before thread 0's fence), count the
+    // split; the last CTA's thread 0 fences again (acquire) and the barrier
+    // passes that on.  One fencing thread instead of 128.
     __syncthreads();
     if (tid == 0) {
+        __threadfence();
         const uint32_t prev = atomicAdd(a.counters + b * a.n_kv + kvh, 1u);
         s_last = prev == (uint32_t)(nsplit - 1);
+        if (s_last) {
+            __threadfence();
+            a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
+        }
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
-    if (tid == 0) a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
 
     // ---- 3. merge the splits (last CTA of this kv head and sequence) -------
     // (m_j, l_j) of up to FT splits at a time in shared memory over the K
