@@ -355,11 +355,99 @@ sample_rows_kernel(const SampArgs a) {
         S.start = 0;
         S.result = -1;
     }
-    __syncthreads();
+    // ---- pass 3a: the first tile by one warp --------------------------------
+    // While cum is small it crosses a binade every few elements, and each
+    // crossing would cost a block-wide round.  So the CTA computes every p of
+    // the first tile into shared memory, and warp 0 scans it in windows of
+    // 256 elements (8 per lane) with warp-wide scans only: the same unit
+    // arithmetic, events and serial fp32 adds as the block rounds below.  The
+    // first window without an event ends it: events have become sparse, and
+    // the block rounds take the rest of the tile faster.
+    {
+        const int t0end = min(kTile, a.vocab);
+        float* const pt = &cbuf[0][0];  // kTile floats
+#pragma unroll
+        for (int h = 0; h < kPerThread / 4; h++) {
+            float v[4];
+            load4(a, lrow, P, tid * kPerThread + 4 * h, v);  // -inf past the vocabulary
+#pragma unroll
+            for (int e = 0; e < 4; e++)
+                pt[tid * kPerThread + 4 * h + e] =
+                    __fmul_rn(pinned_expf_nonpos(__fadd_rn(__fmul_rn(v[e], inv_t), neg_m)), inv);
+        }
+        __syncthreads();
+        if (w == 0) {
+            while (true) {
+                const int start = S.start;
+                if (start >= t0end || S.result >= 0) break;  // warp-uniform
+                const uint32_t ucum = S.ucum, tr = S.tr;
+                const int E = S.E;
+                uint32_t k[kPerThread];
+                bool ser[kPerThread];
+                uint32_t kt = 0;
+#pragma unroll
+                for (int q = 0; q < kPerThread; q++) {
+                    const int i = start + lane * kPerThread + q;
+                    bool tie = false, big = false;
+                    k[q] = 0;
+                    if (i < t0end) classify(pt[i], E, k[q], tie, big);
+                    ser[q] = tie || big;
+                    kt = sat_add(kt, ser[q] ? kSat : k[q]);
+                }
+                uint32_t inc = kt;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
+                    if (lane >= off) inc = sat_add(inc, o);
+                }
+                const uint32_t all = __shfl_sync(0xffffffffu, inc, 31);
+                uint32_t excl = __shfl_up_sync(0xffffffffu, inc, 1);
+                if (lane == 0) excl = 0;
+                uint32_t run = sat_add(ucum, excl), before = run, ev = kNoEvent;
+                int evq = 0;
+#pragma unroll
+                for (int q = 0; q < kPerThread; q++) {
+                    const int i = start + lane * kPerThread + q;
+                    if (i >= t0end || ev != kNoEvent) continue;
+                    if (ser[q]) { ev = (uint32_t)i << 1; before = run; evq = q; continue; }
+                    const uint32_t nr = sat_add(run, k[q]);
+                    if (nr >= kBinadeUnits) { ev = (uint32_t)i << 1; before = run; evq = q; continue; }
+                    if (nr >= tr) { ev = ((uint32_t)i << 1) | 1u; evq = q; continue; }
+                    run = nr;
+                }
+                const uint32_t gev = __reduce_min_sync(0xffffffffu, ev);
+                if (gev == kNoEvent) {
+                    if (lane == 0) {
+                        S.ucum = ucum + all;  // no crossing: exact and < 2^24
+                        S.start = min(start + kWarp * kPerThread, t0end);
+                    }
+                    break;
+                }
+                if (ev == gev) {  // owner of the first event
+                    const int i = (int)(gev >> 1);
+                    if (gev & 1u) {
+                        S.result = i;
+                    } else {
+                        float pe = pt[start + lane * kPerThread];
+#pragma unroll
+                        for (int q = 1; q < kPerThread; q++)
+                            if (q == evq) pe = pt[start + lane * kPerThread + q];
+                        const float cum_prev =
+                            __fmul_rn(__fmul_rn((float)before, pow2i(E - 23 + 64)), pow2i(-64));
+                        const float cum = __fadd_rn(cum_prev, pe);
+                        if (cum >= r) S.result = i;
+                        else { set_binade(S, cum, r, ln_2inv); S.start = i + 1; }
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+    }
     float* cb = cbuf[w];
     uint16_t* ci = cidx[w];
     const int ntiles = (a.vocab + kTile - 1) / kTile;
-    for (int tile = 0; tile < ntiles; tile++) {
+    for (int tile = S.start / kTile; tile < ntiles && S.result < 0; tile++) {
         const int tbase = tile * kTile;
         const int base = tbase + tid * kPerThread;
         float d[kPerThread];
