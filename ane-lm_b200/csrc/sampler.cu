@@ -70,7 +70,7 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) {
 struct RowSmem {
     float red_f[kVirtThreads / kWarp];
     uint32_t red_u[kSampWarps];
-    uint32_t wscan[kSampWarps];
+    uint32_t wscan[2][kSampWarps];  // warp totals, alternating by round
     float bcast_f;
     // CDF state
     uint32_t ucum;   // running sum in units of U
@@ -447,6 +447,14 @@ sample_rows_kernel(const SampArgs a) {
     float* cb = cbuf[w];
     uint16_t* ci = cidx[w];
     const int ntiles = (a.vocab + kTile - 1) / kTile;
+    // The scan state, held identically by every thread: a tile without an
+    // event (no serial element, no crossing, no hit -- read off the block
+    // total alone) advances it locally with no further barrier; after an
+    // event the owner updates S and every thread reloads it.
+    uint32_t st_ucum = S.ucum, st_tr = S.tr;
+    int st_E = S.E, st_start = S.start;
+    float st_td = S.td;
+    int rp = 0;  // round parity: which wscan buffer
     for (int tile = S.start / kTile; tile < ntiles && S.result < 0; tile++) {
         const int tbase = tile * kTile;
         const int base = tbase + tid * kPerThread;
@@ -459,7 +467,7 @@ sample_rows_kernel(const SampArgs a) {
             for (int e = 0; e < 4; e++) d[4 * h + e] = __fadd_rn(__fmul_rn(v[e], inv_t), neg_m);
         }
         // compact the significant elements of the warp, in element order
-        const float td0 = S.td;
+        const float td0 = st_td;
         uint32_t sig = 0;
 #pragma unroll
         for (int e = 0; e < kPerThread; e++)
@@ -497,9 +505,9 @@ sample_rows_kernel(const SampArgs a) {
 
         const int tile_end = min(tbase + kTile, a.vocab);
         while (true) {
-            const uint32_t ucum = S.ucum;
-            const int E = S.E, start = S.start;
-            const uint32_t tr = S.tr;
+            const uint32_t ucum = st_ucum;
+            const int E = st_E, start = st_start;
+            const uint32_t tr = st_tr;
             uint32_t k[kPerThread];
             bool ser[kPerThread], valid[kPerThread];
             uint32_t kt = 0;
@@ -523,16 +531,25 @@ sample_rows_kernel(const SampArgs a) {
                 const uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
                 if (lane >= off) inc = sat_add(inc, o);
             }
-            if (lane == 31) S.wscan[w] = inc;  // warp total
+            if (lane == 31) S.wscan[rp][w] = inc;  // warp total
             __syncthreads();
             // prefix over the warp totals: lane j holds warp j's total
-            uint32_t wt = lane < kSampWarps ? S.wscan[lane] : 0u;
+            uint32_t wt = lane < kSampWarps ? S.wscan[rp][lane] : 0u;
+            rp ^= 1;
 #pragma unroll
             for (int off = 1; off < kSampWarps; off <<= 1) {
                 const uint32_t o = __shfl_up_sync(0xffffffffu, wt, off);
                 if (lane >= off) wt = sat_add(wt, o);
             }
             const uint32_t all = __shfl_sync(0xffffffffu, wt, kSampWarps - 1);
+            const uint32_t tot = sat_add(ucum, all);
+            if (tot < tr && tot < kBinadeUnits) {
+                // no event in the tile (a serial element saturates `all`):
+                // the same update in every thread, no barrier
+                st_ucum = tot;  // exact and < 2^24
+                st_start = tile_end;
+                break;
+            }
             uint32_t wpre = __shfl_sync(0xffffffffu, wt, (w + 31) & 31);
             if (w == 0) wpre = 0;
             uint32_t excl = __shfl_up_sync(0xffffffffu, inc, 1);
@@ -557,12 +574,9 @@ sample_rows_kernel(const SampArgs a) {
             __syncthreads();
             const uint32_t gev =
                 __reduce_min_sync(0xffffffffu, lane < kSampWarps ? S.red_u[lane] : kNoEvent);
-            if (gev == kNoEvent) {
-                if (tid == 0) {
-                    S.ucum = ucum + all;  // no crossing: exact and < 2^24
-                    S.start = tile_end;
-                }
-                __syncthreads();
+            if (gev == kNoEvent) {  // cannot happen (the test above took those tiles); kept safe
+                st_ucum = ucum + all;
+                st_start = tile_end;
                 break;
             }
             if (ev == gev) {  // owner of the first event
@@ -584,6 +598,11 @@ sample_rows_kernel(const SampArgs a) {
             }
             __syncthreads();
             if (S.result >= 0) break;
+            st_ucum = S.ucum;
+            st_tr = S.tr;
+            st_E = S.E;
+            st_start = S.start;
+            st_td = S.td;
         }
         if (S.result >= 0) break;
     }
