@@ -60,6 +60,47 @@ def _p(v):
     lambda L: L.ane_cuda_sample_rows(_p(16), 2, 8, 8, _p(16), None, 4, _p(16), 0.6, 1.2, 256,
                                      0.1, _p(16), None),
     lambda L: L.ane_cuda_read_status_flags(None, 0),
+    # decode attention: bad dtype, heads not a multiple of kv heads, null
+    # pointer, output stride below the heads, negative max_len
+    lambda L: L.ane_cuda_decode_attention(7, _p(16), 2048, _p(16), 2048, 128, _p(16), _p(16),
+                                          1 << 20, _p(16), _p(16), 1024, 1, 16, 8, 128, 64, None,
+                                          0, None),
+    lambda L: L.ane_cuda_decode_attention(0, _p(16), 2048, _p(16), 2048, 128, _p(16), _p(16),
+                                          1 << 20, _p(16), _p(16), 1024, 1, 12, 8, 128, 64, None,
+                                          0, None),
+    lambda L: L.ane_cuda_decode_attention(0, None, 2048, _p(16), 2048, 128, _p(16), _p(16),
+                                          1 << 20, _p(16), _p(16), 1024, 1, 16, 8, 128, 64, None,
+                                          0, None),
+    lambda L: L.ane_cuda_decode_attention(0, _p(16), 100, _p(16), 2048, 128, _p(16), _p(16),
+                                          1 << 20, _p(16), _p(16), 1024, 1, 16, 8, 128, 64, None,
+                                          0, None),
+    lambda L: L.ane_cuda_decode_attention(0, _p(16), 2048, _p(16), 2048, 128, _p(16), _p(16),
+                                          1 << 20, _p(16), _p(16), 1024, 1, 16, 8, 128, -1, None,
+                                          0, None),
+    # a caller workspace that is too small
+    lambda L: L.ane_cuda_decode_attention(0, _p(16), 2048, _p(16), 2048, 128, _p(16), _p(16),
+                                          1 << 20, _p(16), _p(16), 1024, 1, 16, 8, 128, 1024,
+                                          _p(256), 16, None),
+    # the allocation-free form: more split scratch than its fixed array
+    lambda L: L.ane_cuda_decode_attention_static(0, _p(16), 4096, _p(16), 4096, 128, _p(16),
+                                                 _p(16), 1 << 22, _p(16), _p(16), 8192, 64, 32, 8,
+                                                 128, 8192, None),
+    lambda L: L.ane_cuda_qk_norm_rope_kv(1, _p(16), _p(16), None, 512, 512, 512, 128, 128, 128, 2,
+                                         1, 128, _p(16), _p(16), _p(16), _p(16), _p(16), 0, _p(16),
+                                         64, 1, 1e6, 1e-6, None),
+    lambda L: L.ane_cuda_qk_norm_rope_kv(1, _p(16), _p(16), _p(16), 512, 512, 512, 128, 128, 128, 2,
+                                         1, 128, _p(16), _p(16), _p(16), _p(16), _p(16), 0, _p(16),
+                                         0, 1, 1e6, 1e-6, None),
+    lambda L: L.ane_cuda_rmsnorm_gated(0, _p(16), 128, _p(16), 64, _p(16), 128, _p(16), 2, 128,
+                                       1e-6, None),
+    lambda L: L.ane_cuda_rmsnorm_gated(0, _p(16), 128, _p(16), 128, None, 128, _p(16), 2, 128,
+                                       1e-6, None),
+    lambda L: L.ane_cuda_l2_normalize(0, None, 128, 2, 128, 1.0, None),
+    lambda L: L.ane_cuda_l2_normalize(9, _p(16), 128, 2, 128, 1.0, None),
+    lambda L: L.ane_cuda_bf16_to_f32(_p(16), _p(16), -1, 1, None),
+    lambda L: L.ane_cuda_ane_pack(2, _p(16), _p(16), 8, 4, 8, 32, None),
+    lambda L: L.ane_cuda_ane_pack(0, _p(16), _p(16), 8, 4, 8, 0, None),
+    lambda L: L.ane_cuda_ane_unpack(_p(16), 4, _p(16), 4, 8, 32, None),
 ])
 def test_invalid_arguments_rejected_on_host(ane, call):
     L = ane.lib()
@@ -74,6 +115,41 @@ def test_zero_sized_calls_are_no_ops(ane):
     assert L.ane_cuda_silu_mul(1, None, 8, None, 8, None, 8, 0, 8, None) == A.OK
     assert L.ane_cuda_sample_rows(None, 0, 8, 8, None, None, 0, None, 0.6, 1.2, 256, 0.1, None,
                                   None) == A.OK
+
+
+def test_zero_sized_calls_of_the_next_rows(ane):
+    L = ane.lib()
+    assert L.ane_cuda_decode_attention(0, _p(16), 2048, _p(16), 2048, 128, _p(16), _p(16), 1 << 20,
+                                       _p(16), _p(16), 1024, 0, 16, 8, 128, 1024, None, 0,
+                                       None) == A.OK
+    assert L.ane_cuda_ane_pack(0, None, None, 8, 0, 8, 32, None) == A.OK
+    assert L.ane_cuda_ane_unpack(None, 8, None, 0, 8, 32, None) == A.OK
+    assert L.ane_cuda_rmsnorm_gated(0, None, 8, None, 8, None, 8, None, 0, 8, 1e-6, None) == A.OK
+    assert L.ane_cuda_l2_normalize(0, None, 8, 0, 8, 1.0, None) == A.OK
+    assert L.ane_cuda_bf16_to_f32(None, None, 0, 0, None) == A.OK
+
+
+@pytest.mark.parametrize("head_dim,heads,kv", [(96, 16, 8), (128, 32, 2)])
+def test_decode_attention_unsupported_shapes(ane, head_dim, heads, kv):
+    """head_dim other than 64/128/256, or more than 8 q heads per kv head."""
+    L = ane.lib()
+    st = L.ane_cuda_decode_attention(0, _p(16), heads * head_dim, _p(16), heads * head_dim,
+                                     head_dim, _p(16), _p(16), 1 << 22, _p(16), _p(16), 1024, 1,
+                                     heads, kv, head_dim, 64, None, 0, None)
+    assert st == A.ERR_UNSUPPORTED
+
+
+def test_workspace_size_rule(ane):
+    """No workspace with one split (max_len <= 64); counters + (m, l) + o per
+    split otherwise, each 256-byte aligned."""
+    L = ane.lib()
+    assert L.ane_cuda_decode_attention_workspace_size(4, 16, 8, 128, 64) == 0
+    n = L.ane_cuda_decode_attention_workspace_size(4, 16, 8, 128, 4096)
+    splits = 4096 // 64
+    r = lambda v: (v + 255) // 256 * 256  # noqa: E731
+    assert n == r(4 * 8 * 4) + r(4 * 16 * splits * 2 * 4) + r(4 * 16 * splits * 128 * 4)
+    assert L.ane_cuda_decode_attention_workspace_size(-1, 16, 8, 128, 64) == -1
+    assert L.ane_cuda_decode_attention_static_capacity() == 16 << 20
 
 
 def test_unsupported_window_is_reported(ane):
