@@ -121,6 +121,45 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return y;
 }
 
+// Packed fp32 pairs (sm_100 f32x2): two independent IEEE operations per
+// instruction, each rounded to nearest even with subnormals kept -- the same
+// bits as __fmul_rn / __fadd_rn / __fsub_rn / __fmaf_rn element by element
+// (checked on the B200 over 2^20 random pairs, specials included).
+// The pairs are built and split inside the asm (mov.b64 {lo, hi}), so no
+// value is reinterpreted through a pointer.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " sub.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+
 // pinned_expf for x <= 0 (softmax arguments x - max), without branches:
 // the same operations in the same order as pinned_expf, so the same bits for
 // every x in [-inf, 0]; the two-step subnormal scaling is selected, not
@@ -142,6 +181,32 @@ __device__ __forceinline__ float pinned_expf_nonpos(float x) {
     float y = __fmul_rn(p, pow2i(sub ? ki + 64 : ki));
     y = sub ? __fmul_rn(y, pow2i(-64)) : y;
     return x < -104.0f ? 0.0f : y;
+}
+
+// pinned_expf_nonpos of two arguments: the same operations, the multiplies
+// and fmas two at a time (packed f32x2, the same bits element by element).
+// No packed multiply here feeds an add, so nothing can be contracted.
+__device__ __forceinline__ float2 pinned_expf_nonpos2(float2 x) {
+    const float2 xc = make_float2(fmaxf(x.x, -104.0f), fmaxf(x.y, -104.0f));
+    const float2 t = mul2_rn(xc, make_float2(1.44269502162933349609375f, 1.44269502162933349609375f));
+    const float2 k = make_float2(rintf(t.x), rintf(t.y));
+    const float2 nk = make_float2(-k.x, -k.y);
+    float2 r = fma2_rn(nk, make_float2(0.693147182464599609375f, 0.693147182464599609375f), xc);
+    r = fma2_rn(nk, make_float2(-1.904654212125933608e-09f, -1.904654212125933608e-09f), r);
+    const auto c2 = [](float c) { return make_float2(c, c); };
+    float2 p = fma2_rn(c2(0.00019841270113829523324966431f), r, c2(0.0013888889225199818611145020f));
+    p = fma2_rn(p, r, c2(0.0083333337679505348205566406f));
+    p = fma2_rn(p, r, c2(0.041666667908430099487304688f));
+    p = fma2_rn(p, r, c2(0.16666667163372039794921875f));
+    p = fma2_rn(p, r, c2(0.5f));
+    p = fma2_rn(p, r, c2(1.0f));
+    p = fma2_rn(p, r, c2(1.0f));
+    const int k0 = (int)k.x, k1 = (int)k.y;
+    const bool s0 = k0 < -126, s1 = k1 < -126;
+    float2 y = mul2_rn(p, make_float2(pow2i(s0 ? k0 + 64 : k0), pow2i(s1 ? k1 + 64 : k1)));
+    y.x = s0 ? __fmul_rn(y.x, pow2i(-64)) : y.x;
+    y.y = s1 ? __fmul_rn(y.y, pow2i(-64)) : y.y;
+    return make_float2(x.x < -104.0f ? 0.0f : y.x, x.y < -104.0f ? 0.0f : y.y);
 }
 
 // ---------------------------------------------------------------------

@@ -328,17 +328,28 @@ sample_rows_kernel(const SampArgs a) {
         float va[4], vb[4];
         if (ga < ngroups) load4(a, lrow, P, ga * 4, va);
         if (gb < ngroups) load4(a, lrow, P, gb * 4, vb);
+        // the exps two at a time (packed), the adds in order
         if (ga < ngroups) {
+            float d[4], e[4];
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                if (ga * 4 + e < a.vocab)
-                    acc_lo = __fadd_rn(acc_lo, pinned_expf_nonpos(__fadd_rn(__fmul_rn(va[e], inv_t), neg_m)));
+            for (int j = 0; j < 4; j++) d[j] = __fadd_rn(__fmul_rn(va[j], inv_t), neg_m);
+            const float2 e01 = pinned_expf_nonpos2(make_float2(d[0], d[1]));
+            const float2 e23 = pinned_expf_nonpos2(make_float2(d[2], d[3]));
+            e[0] = e01.x; e[1] = e01.y; e[2] = e23.x; e[3] = e23.y;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (ga * 4 + j < a.vocab) acc_lo = __fadd_rn(acc_lo, e[j]);
         }
         if (gb < ngroups) {
+            float d[4], e[4];
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                if (gb * 4 + e < a.vocab)
-                    acc_hi = __fadd_rn(acc_hi, pinned_expf_nonpos(__fadd_rn(__fmul_rn(vb[e], inv_t), neg_m)));
+            for (int j = 0; j < 4; j++) d[j] = __fadd_rn(__fmul_rn(vb[j], inv_t), neg_m);
+            const float2 e01 = pinned_expf_nonpos2(make_float2(d[0], d[1]));
+            const float2 e23 = pinned_expf_nonpos2(make_float2(d[2], d[3]));
+            e[0] = e01.x; e[1] = e01.y; e[2] = e23.x; e[3] = e23.y;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (gb * 4 + j < a.vocab) acc_hi = __fadd_rn(acc_hi, e[j]);
         }
     }
     const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
@@ -371,9 +382,12 @@ sample_rows_kernel(const SampArgs a) {
             float v[4];
             load4(a, lrow, P, tid * kPerThread + 4 * h, v);  // -inf past the vocabulary
 #pragma unroll
-            for (int e = 0; e < 4; e++)
-                pt[tid * kPerThread + 4 * h + e] =
-                    __fmul_rn(pinned_expf_nonpos(__fadd_rn(__fmul_rn(v[e], inv_t), neg_m)), inv);
+            for (int e = 0; e < 4; e += 2) {
+                const float2 ex = pinned_expf_nonpos2(make_float2(__fadd_rn(__fmul_rn(v[e], inv_t), neg_m),
+                                                                  __fadd_rn(__fmul_rn(v[e + 1], inv_t), neg_m)));
+                pt[tid * kPerThread + 4 * h + e] = __fmul_rn(ex.x, inv);
+                pt[tid * kPerThread + 4 * h + e + 1] = __fmul_rn(ex.y, inv);
+            }
         }
         __syncthreads();
         if (w == 0) {
@@ -489,7 +503,14 @@ sample_rows_kernel(const SampArgs a) {
                 pos++;
             }
         __syncwarp();
-        for (int j = lane; j < nw; j += kWarp) cb[j] = __fmul_rn(pinned_expf_nonpos(cb[j]), inv);
+        // exps of the compacted items, two per lane at a time (packed)
+        for (int j = lane; j < nw; j += 2 * kWarp) {
+            const int j2 = j + kWarp < nw ? j + kWarp : j;
+            const float2 ex = pinned_expf_nonpos2(make_float2(cb[j], cb[j2]));
+            const float p0 = __fmul_rn(ex.x, inv), p1 = __fmul_rn(ex.y, inv);
+            cb[j] = p0;  // lane l owns items l + 64m and l + 32 + 64m
+            if (j2 != j) cb[j2] = p1;
+        }
         __syncwarp();
         // lane l takes the contiguous items [l*c, l*c + c)
         const int c = (nw + kWarp - 1) / kWarp;
