@@ -265,6 +265,21 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte
+// aligned), completed by cp_async_commit / cp_async_wait_pending
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// waits until at most n (0-3) of this thread's latest commit groups are pending
+__device__ __forceinline__ void cp_async_wait_pending(int n) {
+    switch (n) {
+        case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+        case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+        case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+        default: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    }
+}
 // orders this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (bulk copy) accesses
 __device__ __forceinline__ void fence_proxy_async() {

@@ -131,6 +131,8 @@ int attention_args(int dtype, void* out, int64_t out_stride, const void* q, int6
     a->n_kv = n_kv_heads;
     a->max_len = max_len;
     a->max_splits = splits_of(max_len);
+    a->chunks = 1;  // set per launch
+    a->stages = 0;
     a->scale = 1.0f / sqrtf((float)head_dim);  // core/cpu_ops.cpp:182
     a->counters = nullptr;
     a->part_ml = nullptr;

@@ -5,7 +5,8 @@
 // One query token per sequence.  The keys of a sequence are cut into splits
 // of kAttnKeys; one CTA takes one (split, kv head, sequence) and serves all
 // the q heads of that kv head, so every K and V row is read from HBM once.
-// The CTA
+// (The 16-bit kernel further down takes several consecutive splits per CTA
+// through a copy pipeline.)  The fp32 kernel's CTA
 //   1. stages its K rows and V rows in shared memory with one bulk copy per
 //      row (TMA engine, 16-byte aligned rows; the ring wrap is per row),
 //      on two mbarriers so the score pass starts while V is in flight;
@@ -15,8 +16,8 @@
 //      workspace, and the CTA that finishes last for its (kv head,
 //      sequence) -- an atomic counter -- combines the splits and writes the
 //      output, then resets the counter to zero.
-// Every summation order is fixed, so a CPU restatement doing the same
-// operations in the same order reproduces the result bit for bit:
+// Every summation order of the fp32 kernel is fixed, so a CPU restatement
+// doing the same operations in the same order reproduces it bit for bit:
 //   dot   EPL = max(16 B / element, head_dim / 32) consecutive elements per
 //         lane, GL = head_dim / EPL lanes per key: an fmaf chain per lane,
 //         then an xor butterfly over the GL lanes;
@@ -29,6 +30,7 @@
 // exp is the pinned pinned_expf of ane_common.cuh.
 #pragma once
 
+#include <atomic>
 #include <type_traits>
 
 #include "ane_common.cuh"
@@ -56,6 +58,8 @@ struct AttnArgs {
     int capacity;
     int n_heads, n_kv;
     int max_len, max_splits;
+    int chunks;            // 64-key chunks per CTA (16-bit kernel; 1 for fp32)
+    int stages;            // copy stages per warp (16-bit kernel)
     float scale;           // 1 / sqrtf(head_dim)
     uint32_t* counters;    // [batch][n_kv], zero between calls
     float* part_ml;        // [batch][n_heads][max_splits][2]
@@ -505,17 +509,32 @@ decode_attention_kernel(const AttnArgs a) {
 
 
 // ---------------------------------------------------------------------------
-// 16-bit caches: the same split structure with the two contractions on the
-// tensor cores (mma.sync m16n8k16, fp32 accumulation).  Rows of the MMA are
+// 16-bit caches: the two contractions on the tensor cores (mma.sync
+// m16n8k16, fp32 accumulation), and a pipelined split.  Rows of the MMA are
 // the kv head's q heads (G <= 8 of 16; the rest are zero), so one warp's
-// scores for its 16 keys are two MMA tiles per 16 dims, and P.V for those
-// keys is one 16-deep k-step per 8 dims.  The exps stay in registers and are
-// the A operand of P.V directly (the accumulator layout of the first MMA is
-// the operand layout of the second).  P is split into a high and a low part
-// in the cache's type (fp16 scaled by 2^12 so the low part stays normal), so
+// scores for 16 keys are two MMA tiles per 16 dims, and P.V for those keys
+// is one 16-deep k-step per 8 dims.  The exps stay in registers and are the
+// A operand of P.V directly (the accumulator layout of the first MMA is the
+// operand layout of the second).  P is split into a high and a low part in
+// the cache's type (fp16 scaled by 2^12 so the low part stays normal), so
 // P.V keeps about 16 (bf16) / 22 (fp16) significant bits of each weight.
-// The MMA's internal summation order is the hardware's: results agree with
-// the fp32 CUDA-core order to within the output type's rounding (one unit).
+//
+// A CTA takes `chunks` consecutive 64-key chunks of one (kv head,
+// sequence); warp w takes keys 16w .. 16w+15 of every chunk.  Each warp
+// runs its own copy pipeline: its lanes copy the chunk's K and V rows in
+// 16-byte pieces (cp.async; the ring wrap is per row) into a ring of
+// `stages` buffers, one commit group per chunk, so the copies of the next
+// chunks are in flight while the current one is computed, and no block
+// barrier is taken until the end of the split.  (One bulk copy per 256-byte
+// row, as in the fp32 kernel, held this kernel to about 60% of the HBM
+// bandwidth: many small bulk copies cost more than the same bytes in
+// 16-byte pieces.)  The warp keeps a running
+// max m, sum l and o per head (online softmax: when m grows, l and o are
+// scaled by exp(m_old - m_new)); at the end the four warps are merged with
+// f_w = exp(m_w - M) into the split's (M, L, O), which attn_finish writes
+// or merges like the fp32 kernel's.  The summation orders differ from the
+// fp32 kernel's (the MMA's internal order is the hardware's): results
+// agree with the fp32 order to within the output type's rounding.
 // K and V rows sit in shared memory with a 16-byte pad per row, which makes
 // the fragment loads (32-bit loads for K, ldmatrix.trans for V) free of bank
 // conflicts.
@@ -565,10 +584,21 @@ __device__ __forceinline__ float high_f(uint32_t v) {
 template <int HD>
 __host__ __device__ constexpr int attn_mma_rs() { return HD + 8; }  // padded row, elements
 
+constexpr int kAttnWarpKeys = kAttnKeys / kAttnWarps;  // keys of a warp in one chunk
+constexpr int kAttnMaxStages = 4;
+
 template <int HD>
-__host__ __device__ constexpr size_t attn_mma_smem_bytes() {
-    return 2 * (size_t)kAttnKeys * attn_mma_rs<HD>() * 2;  // K and V rows, 16-bit
+__host__ __device__ constexpr size_t attn_mma_stage_bytes() {  // one warp's K and V rows of a chunk
+    return 2 * (size_t)kAttnWarpKeys * attn_mma_rs<HD>() * 2;
 }
+template <int HD>
+__host__ __device__ constexpr size_t attn_mma_smem_bytes(int stages) {
+    return (size_t)kAttnWarps * stages * attn_mma_stage_bytes<HD>();
+}
+// ring stages per warp: two to three chunks in flight per warp and two CTAs
+// per SM (one at head_dim 256) cover the HBM latency
+template <int HD>
+__host__ __device__ constexpr int attn_mma_max_stages() { return HD <= 64 ? 4 : 3; }
 
 template <typename T, int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads)
@@ -577,18 +607,19 @@ decode_attention_mma_kernel(const AttnArgs a) {
     static_assert(sizeof(S) == 2, "16-bit caches");
     static_assert(G <= 8, "at most 8 q heads per kv head");
     constexpr int RS = attn_mma_rs<HD>();
+    constexpr int WK = kAttnWarpKeys;
+    constexpr int STAGE = 2 * WK * RS;  // elements: K rows, then V rows
     constexpr uint32_t ROW = HD * sizeof(S);
     constexpr int KSTEPS = HD / 16;
     constexpr bool F16S = std::is_same<T, F16>::value;
     constexpr float PSCALE = F16S ? 4096.0f : 1.0f;  // 2^12: fp16 low parts stay normal
-    static_assert((size_t)kAttnWarps * G * HD * sizeof(float) <= (size_t)kAttnKeys * RS * sizeof(S),
-                  "warp partials must fit over the K rows");
-    static_assert(attn_rows_bytes<T, HD>() <= attn_mma_smem_bytes<HD>(), "merge tile");
+    static_assert(WK == 16, "one 16-deep k-step of P.V per warp and chunk");
+    // the warp partials and the merge tile of attn_finish fit in one stage set
+    static_assert((size_t)kAttnWarps * G * HD * sizeof(float) <= attn_mma_smem_bytes<HD>(1),
+                  "warp partials");
+    static_assert(attn_rows_bytes<T, HD>() <= attn_mma_smem_bytes<HD>(1), "merge tile");
     extern __shared__ __align__(16) unsigned char smem[];
-    S* const sK = reinterpret_cast<S*>(smem);
-    S* const sV = sK + kAttnKeys * RS;
-    float* const s_red = reinterpret_cast<float*>(smem);  // [warp][G][HD], over the K rows
-    __shared__ __align__(8) uint64_t bars[2];
+    float* const s_red = reinterpret_cast<float*>(smem);  // [warp][G][HD], after the pipelines
     __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
     __shared__ float s_wm[G][kAttnWarps], s_wl[G][kAttnWarps];
     __shared__ int s_last;
@@ -610,39 +641,46 @@ decode_attention_mma_kernel(const AttnArgs a) {
         }
         return;
     }
-    const int nsplit = (len + kAttnKeys - 1) / kAttnKeys;
+    const int nchunk = (len + kAttnKeys - 1) / kAttnKeys;
+    const int nsplit = (nchunk + a.chunks - 1) / a.chunks;
     if (split >= nsplit) return;
-    const int t0 = split * kAttnKeys;
-    const int n = min(kAttnKeys, len - t0);
+    const int c0 = split * a.chunks;              // first chunk of this CTA
+    const int nc = min(nchunk - c0, a.chunks);    // its chunks, >= 1
+    const int ns = a.stages;                      // 1 .. kAttnMaxStages
 
-    // ---- 1. stage K and V rows (padded) ------------------------------------
-    if (tid == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    if (tid == 0) {
-        mbar_expect_tx(&bars[0], (uint32_t)n * ROW);
-        mbar_expect_tx(&bars[1], (uint32_t)n * ROW);
-    }
-    __syncthreads();  // byte counts registered before any copy is issued
-    {
-        const int i = tid & (kAttnKeys - 1);  // threads 0-63 copy K rows, 64-127 V rows
-        if (i < n) {
-            int slot = start + t0 + i;  // ring position (models/llm/qwen3.cpp:190-204)
-            if (slot >= a.capacity) slot -= a.capacity;
-            const int64_t off = b * a.cache_stride + ((int64_t)slot * a.n_kv + kvh) * HD;
-            if (tid < kAttnKeys)
-                bulk_load(sK + i * RS, static_cast<const S*>(a.k_cache) + off, ROW, &bars[0]);
-            else
-                bulk_load(sV + i * RS, static_cast<const S*>(a.v_cache) + off, ROW, &bars[1]);
-        } else if (tid >= kAttnKeys) {
-            // V rows past the keys enter P.V with weight 0: make them finite
-            uint4* z = reinterpret_cast<uint4*>(sV + i * RS);
-            for (int c = 0; c < (int)(ROW / 16); c++) z[c] = make_uint4(0u, 0u, 0u, 0u);
+    // ---- the warp's copy ring -----------------------------------------------
+    S* const ring = reinterpret_cast<S*>(smem) + (size_t)w * ns * STAGE;
+    constexpr int CPR = ROW / 16;  // 16-byte pieces per row
+    const S* const kbase = static_cast<const S*>(a.k_cache) + b * a.cache_stride + (int64_t)kvh * HD;
+    const S* const vbase = static_cast<const S*>(a.v_cache) + b * a.cache_stride + (int64_t)kvh * HD;
+    // the warp's keys of chunk j of the CTA: first key, and how many exist
+    auto warp_keys = [&](int j, int& kb) {
+        kb = (c0 + j) * kAttnKeys + WK * w;
+        return min(WK, max(0, len - kb));
+    };
+    // chunk j into stage st: 16-byte asynchronous copies, CPR consecutive
+    // lanes on the pieces of a key's K row and V row (rows 0-15 K, 16-31 V),
+    // one commit group per chunk (an empty one past the last chunk keeps
+    // the count)
+    static_assert(CPR <= kWarp && kWarp % CPR == 0, "row pieces per lane");
+    const int px = lane % CPR;
+    auto issue = [&](int j, int st) {
+        int kb;
+        const int nw = j < nc ? warp_keys(j, kb) : 0;
+        S* const dst = ring + st * STAGE + 8 * px;
+#pragma unroll 4
+        for (int key = lane / CPR; key < WK; key += kWarp / CPR) {
+            if (key < nw) {
+                int slot = start + kb + key;  // ring position (models/llm/qwen3.cpp:190-204)
+                if (slot >= a.capacity) slot -= a.capacity;
+                const int64_t off = (int64_t)slot * a.n_kv * HD + 8 * px;
+                cp_async16(dst + key * RS, kbase + off);
+                cp_async16(dst + (WK + key) * RS, vbase + off);
+            }
         }
-    }
+        cp_async_commit();
+    };
+    for (int j = 0; j < ns; j++) issue(j, j);
 
     // q fragments (rows = heads gid < G; others zero), loaded while the copies fly
     uint32_t qa[KSTEPS][2];
@@ -657,94 +695,138 @@ decode_attention_mma_kernel(const AttnArgs a) {
         }
     }
 
-    if (!__syncthreads_and(mbar_wait_bounded(&bars[0], 0))) {
-        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
-        return;
-    }
-
-    // ---- 2a. scores: warp w takes keys 16w .. 16w+15 (two 8-key tiles) ----
-    float sc[2][4];
-#pragma unroll
-    for (int nb = 0; nb < 2; nb++) {
-        sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
-        const S* kr = sK + (16 * w + 8 * nb + gid) * RS + 2 * tq;
-#pragma unroll
-        for (int ks = 0; ks < KSTEPS; ks++) {
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks + 8);
-            mma16816<T>(sc[nb], qa[ks][0], qa[ks][1], b0, b1);
-        }
-    }
-    // this thread: head gid, keys 16w + 2tq + {0, 1, 8, 9}
-    const int kbase = 16 * w + 2 * tq;
-    float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
-    const int koff[4] = {0, 1, 8, 9};
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        x[i] = kbase + koff[i] < n ? __fmul_rn(x[i], a.scale) : -INFINITY;
-        mx = fmaxf(mx, x[i]);
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    if (tq == 0 && gid < G) s_wm[gid][w] = mx;
-    __syncthreads();
-    float e[4], es = 0.0f;
-    {
-        const int g = gid < G ? gid : 0;
-        const float m = fmaxf(fmaxf(s_wm[g][0], s_wm[g][1]), fmaxf(s_wm[g][2], s_wm[g][3]));
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            e[i] = (gid < G && kbase + koff[i] < n) ? pinned_expf(__fsub_rn(x[i], m)) : 0.0f;
-            es = __fadd_rn(es, e[i]);
-        }
-    }
-    es = __fadd_rn(es, __shfl_xor_sync(0xffffffffu, es, 1));
-    es = __fadd_rn(es, __shfl_xor_sync(0xffffffffu, es, 2));
-    if (tq == 0 && gid < G) s_wl[gid][w] = es;
-    // P as the A operand of P.V: high and low parts
-    uint32_t ph[2], pl[2];
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-        const float p0 = __fmul_rn(e[2 * j], PSCALE), p1 = __fmul_rn(e[2 * j + 1], PSCALE);
-        ph[j] = pack2<T>(p0, p1);
-        pl[j] = pack2<T>(__fsub_rn(p0, low_f<T>(ph[j])), __fsub_rn(p1, high_f<T>(ph[j])));
-    }
-    if (!__syncthreads_and(mbar_wait_bounded(&bars[1], 0))) {
-        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
-        return;
-    }
-
-    // ---- 2b. P.V over the warp's 16 keys ------------------------------------
-    float o[HD / 8][4];
+    // ---- 2. the chunks: scores, online softmax, P.V --------------------------
+    // this thread: head gid, keys k0 + {0, 1, 8, 9} of the warp's 16
+    const int k0 = 2 * tq;
+    float o[HD / 8][4];  // rows gid (elements 0, 1); rows gid + 8 stay zero
 #pragma unroll
     for (int nb = 0; nb < HD / 8; nb++) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
-    {
-        const int mi = lane >> 3, rr = lane & 7;
-        const S* vb = sV + (16 * w + (mi & 1) * 8 + rr) * RS + (mi >> 1) * 8;
+    float m_run = -INFINITY, l_run = 0.0f;
+    int st = 0;
+    for (int j = 0; j < nc; j++) {
+        cp_async_wait_pending(ns - 1);  // chunk j's group has landed (this lane's copies)
+        __syncwarp();                   // ... and every lane's
+        int kb;
+        const int nw = warp_keys(j, kb);  // warp-uniform
+        if (nw > 0) {
+            const S* const sK = ring + st * STAGE;
+            const S* const sV = sK + WK * RS;
+            float sc[2][4];
 #pragma unroll
-        for (int d0 = 0; d0 < HD; d0 += 16) {
-            uint32_t r[4];
-            ldsm_x4_trans(r, vb + d0);
-            mma16816<T>(o[d0 / 8], ph[0], ph[1], r[0], r[1]);
-            mma16816<T>(o[d0 / 8], pl[0], pl[1], r[0], r[1]);
-            mma16816<T>(o[d0 / 8 + 1], ph[0], ph[1], r[2], r[3]);
-            mma16816<T>(o[d0 / 8 + 1], pl[0], pl[1], r[2], r[3]);
+            for (int nb = 0; nb < 2; nb++) {
+                sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
+                const S* kr = sK + (8 * nb + gid) * RS + k0;
+#pragma unroll
+                for (int ks = 0; ks < KSTEPS; ks++) {
+                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks);
+                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks + 8);
+                    mma16816<T>(sc[nb], qa[ks][0], qa[ks][1], b0, b1);
+                }
+            }
+            // rows past the keys hold stale data: their scores become -inf
+            // by selection, and their V fragments are zeroed below
+            float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
+            const int koff[4] = {0, 1, 8, 9};
+            float cm = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                x[i] = k0 + koff[i] < nw ? __fmul_rn(x[i], a.scale) : -INFINITY;
+                cm = fmaxf(cm, x[i]);
+            }
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
+            const float m_new = fmaxf(m_run, cm);
+            float e[4];
+            {
+                const float2 d01 = make_float2(__fsub_rn(x[0], m_new), __fsub_rn(x[1], m_new));
+                const float2 d23 = make_float2(__fsub_rn(x[2], m_new), __fsub_rn(x[3], m_new));
+                const float2 e01 = pinned_expf_nonpos2(d01), e23 = pinned_expf_nonpos2(d23);
+                // NaN scores stay NaN, as in pinned_expf
+                e[0] = d01.x != d01.x ? d01.x : e01.x;
+                e[1] = d01.y != d01.y ? d01.y : e01.y;
+                e[2] = d23.x != d23.x ? d23.x : e23.x;
+                e[3] = d23.y != d23.y ? d23.y : e23.y;
+            }
+            const float f = pinned_expf(__fsub_rn(m_run, m_new));  // 0 on the first keys
+            l_run = __fmaf_rn(l_run, f, __fadd_rn(__fadd_rn(e[0], e[1]), __fadd_rn(e[2], e[3])));
+            if (__any_sync(0xffffffffu, m_new != m_run)) {
+#pragma unroll
+                for (int nb = 0; nb < HD / 8; nb++) {
+                    o[nb][0] = __fmul_rn(o[nb][0], f);
+                    o[nb][1] = __fmul_rn(o[nb][1], f);
+                }
+            }
+            m_run = m_new;
+            // P as the A operand of P.V: high and low parts
+            uint32_t ph[2], pl[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float p0 = __fmul_rn(e[2 * h], PSCALE), p1 = __fmul_rn(e[2 * h + 1], PSCALE);
+                ph[h] = pack2<T>(p0, p1);
+                pl[h] = pack2<T>(__fsub_rn(p0, low_f<T>(ph[h])), __fsub_rn(p1, high_f<T>(ph[h])));
+            }
+            // ldmatrix.trans gives this thread V[keys kh*8 + k0, +1][dim]:
+            // halves of keys >= nw are zeroed (their weight is 0, the data stale)
+            const int mi = lane >> 3, rr = lane & 7;
+            const S* vb = sV + ((mi & 1) * 8 + rr) * RS + (mi >> 1) * 8;
+            auto pv = [&](auto masked) {
+                uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
+                if constexpr (decltype(masked)::value) {
+                    vm0 = (k0 < nw ? 0x0000ffffu : 0u) | (k0 + 1 < nw ? 0xffff0000u : 0u);
+                    vm1 = (k0 + 8 < nw ? 0x0000ffffu : 0u) | (k0 + 9 < nw ? 0xffff0000u : 0u);
+                }
+#pragma unroll
+                for (int d0 = 0; d0 < HD; d0 += 16) {
+                    uint32_t r[4];
+                    ldsm_x4_trans(r, vb + d0);
+                    if constexpr (decltype(masked)::value) {
+                        r[0] &= vm0;
+                        r[1] &= vm1;
+                        r[2] &= vm0;
+                        r[3] &= vm1;
+                    }
+                    mma16816<T>(o[d0 / 8], ph[0], ph[1], r[0], r[1]);
+                    mma16816<T>(o[d0 / 8], pl[0], pl[1], r[0], r[1]);
+                    mma16816<T>(o[d0 / 8 + 1], ph[0], ph[1], r[2], r[3]);
+                    mma16816<T>(o[d0 / 8 + 1], pl[0], pl[1], r[2], r[3]);
+                }
+            };
+            if (nw == WK)
+                pv(std::integral_constant<bool, false>());
+            else
+                pv(std::integral_constant<bool, true>());
         }
+        __syncwarp();  // every lane is done with stage st
+        issue(j + ns, st);
+        st = st + 1 == ns ? 0 : st + 1;
     }
-    __syncthreads();  // every warp is done with the K rows before s_red overwrites them
+
+    // ---- 3. merge the four warps into the split's (M, L, O) -------------------
+    l_run = __fadd_rn(l_run, __shfl_xor_sync(0xffffffffu, l_run, 1));
+    l_run = __fadd_rn(l_run, __shfl_xor_sync(0xffffffffu, l_run, 2));
+    if (tq == 0 && gid < G) {
+        s_wm[gid][w] = m_run;
+        s_wl[gid][w] = l_run;
+    }
+    // after this barrier the rings are dead (every chunk's copies were waited for)
+    __syncthreads();
     if (gid < G) {
-        constexpr float UNSCALE = 1.0f / PSCALE;
+        const float M = fmaxf(fmaxf(s_wm[gid][0], s_wm[gid][1]), fmaxf(s_wm[gid][2], s_wm[gid][3]));
+        const float fw = __fmul_rn(pinned_expf(__fsub_rn(m_run, M)), 1.0f / PSCALE);
 #pragma unroll
         for (int nb = 0; nb < HD / 8; nb++)
-            *reinterpret_cast<float2*>(s_red + (w * G + gid) * HD + 8 * nb + 2 * tq) =
-                make_float2(__fmul_rn(o[nb][0], UNSCALE), __fmul_rn(o[nb][1], UNSCALE));
+            *reinterpret_cast<float2*>(s_red + (w * G + gid) * HD + 8 * nb + k0) =
+                make_float2(__fmul_rn(o[nb][0], fw), __fmul_rn(o[nb][1], fw));
     }
     if (tid < G) {
-        s_m[tid][0] = fmaxf(s_wm[tid][0], s_wm[tid][1]);
-        s_m[tid][1] = fmaxf(s_wm[tid][2], s_wm[tid][3]);
-        s_l[tid][0] = __fadd_rn(s_wl[tid][0], s_wl[tid][1]);
-        s_l[tid][1] = __fadd_rn(s_wl[tid][2], s_wl[tid][3]);
+        const float M = fmaxf(fmaxf(s_wm[tid][0], s_wm[tid][1]), fmaxf(s_wm[tid][2], s_wm[tid][3]));
+        float lw[kAttnWarps];
+#pragma unroll
+        for (int v = 0; v < kAttnWarps; v++)
+            lw[v] = __fmul_rn(s_wl[tid][v], pinned_expf(__fsub_rn(s_wm[tid][v], M)));
+        s_m[tid][0] = s_m[tid][1] = M;
+        s_l[tid][0] = __fadd_rn(lw[0], lw[1]);
+        s_l[tid][1] = __fadd_rn(lw[2], lw[3]);
     }
     __syncthreads();
     attn_finish<T, HD, G>(a, smem, s_red, s_m, s_l, s_M, s_L, s_last, nsplit, split, kvh, b, out);
@@ -763,22 +845,52 @@ namespace ane {
 template <typename T, int HD, int G>
 int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
     // 16-bit caches: the tensor-core kernel; fp32: the CUDA-core kernel
+    AttnArgs la = a;
     size_t smem;
+    unsigned gx = (unsigned)a.max_splits;
     void (*kern)(AttnArgs);
     if constexpr (sizeof(typename T::storage) == 2) {
-        smem = attn_mma_smem_bytes<HD>();
         kern = decode_attention_mma_kernel<T, HD, G>;
-    } else {
-        smem = attn_smem_bytes<T, HD, G>();
-        kern = decode_attention_kernel<T, HD, G>;
-    }
-    if (smem > 48 * 1024) {
-        const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        constexpr int smax = attn_mma_max_stages<HD>();
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)attn_mma_smem_bytes<HD>(smax));
+        // CTAs resident per SM with full rings (the same on every device of
+        // a process: one query)
+        static std::atomic<int> occ{0};
+        int per_sm = occ.load(std::memory_order_relaxed);
+        if (e == cudaSuccess && per_sm == 0) {
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kAttnThreads,
+                                                              attn_mma_smem_bytes<HD>(smax));
+            if (per_sm < 1) per_sm = 1;
+            occ.store(per_sm, std::memory_order_relaxed);
+        }
         if (e != cudaSuccess)
             return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
+        // Split each (kv head, sequence) into just enough CTAs to fill the
+        // resident slots once: long splits keep the copy rings busy and
+        // leave few partials to merge.
+        const int nchunk = a.max_splits;  // 64-key chunks of the longest sequence
+        const int64_t pairs = batch * a.n_kv, slots = (int64_t)sm_count() * per_sm;
+        int64_t nsplit = pairs >= slots ? 1 : slots / pairs;
+        if (nsplit > nchunk) nsplit = nchunk;
+        la.chunks = (int)((nchunk + nsplit - 1) / nsplit);
+        la.stages = la.chunks < smax ? la.chunks : smax;
+        gx = (unsigned)((nchunk + la.chunks - 1) / la.chunks);
+        smem = attn_mma_smem_bytes<HD>(la.stages);
+    } else {
+        kern = decode_attention_kernel<T, HD, G>;
+        la.chunks = 1;
+        la.stages = 0;
+        smem = attn_smem_bytes<T, HD, G>();
+        if (smem > 48 * 1024) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess)
+                return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
+        }
     }
-    const dim3 grid((unsigned)a.max_splits, (unsigned)a.n_kv, (unsigned)batch);
-    kern<<<grid, kAttnThreads, smem, s>>>(a);
+    const dim3 grid(gx, (unsigned)a.n_kv, (unsigned)batch);
+    kern<<<grid, kAttnThreads, smem, s>>>(la);
     return check_launch("decode_attention");
 }
 

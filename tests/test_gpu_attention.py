@@ -3,8 +3,9 @@ through the C ABI.
 
 fp32 caches: the CUDA-core kernel takes every sum in the oracle's fixed
 order, so the two agree bit for bit.  16-bit caches: the contractions run on
-the tensor cores, whose internal summation order is the hardware's; the fp32
-result is then within about 1e-6 relative of the oracle's, so the stored
+the tensor cores, whose internal summation order is the hardware's, and the
+softmax is taken online over each warp's keys; the fp32 result is then
+within about 1e-6 relative of the oracle's, so the stored
 fp16 / bf16 outputs agree with the oracle's to within one unit in the last
 place (most of them exactly).  Against the reference itself (its
 gqa_attention compiled with the shim, sequential sums) the fp32 output must
@@ -102,6 +103,35 @@ SHAPES = [
 def test_attention_matches_oracle(ane, oracle, dt, shape):
     B, H, hk, hd, cap, starts, lens = shape
     rng = np.random.default_rng(zlib.crc32(repr((B, H, hk, hd, cap, dt)).encode()))
+    q, k, v, st, ln = make_case(rng, B, H, hk, hd, cap, starts, lens, dt)
+    want = oracle.decode_attention(q, k, v, st, ln)
+    got = run_gpu(ane, q, k, v, st, ln, dt)
+    check_against_oracle(got, want, dt, float(np.abs(as_f32(v, dt) if dt != "f32" else v).max()))
+
+
+# Batches large enough that the 16-bit kernel takes several 64-key chunks
+# per CTA: one split per (kv head, sequence) with the copy ring reused many
+# times (first three), or a few splits of several chunks each (last two);
+# lengths ragged from 0 to the capacity, starts anywhere in the ring.
+PIPE_SHAPES = [
+    # B, H, Hk, hd, cap
+    (40, 32, 8, 128, 777),
+    (40, 16, 8, 64, 600),
+    (24, 64, 8, 256, 333),
+    (12, 32, 8, 128, 1000),
+    (8, 32, 8, 128, 2048),
+]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("shape", PIPE_SHAPES, ids=lambda s: f"B{s[0]}H{s[1]}k{s[2]}d{s[3]}c{s[4]}")
+def test_attention_long_splits(ane, oracle, dt, shape):
+    B, H, hk, hd, cap = shape
+    rng = np.random.default_rng(zlib.crc32(repr(("pipe", shape, dt)).encode()))
+    lens = rng.integers(1, cap + 1, size=B)
+    special = [0, 1, 64, 65, cap, cap - 1]
+    lens[:len(special)] = special
+    starts = rng.integers(0, cap, size=B)
     q, k, v, st, ln = make_case(rng, B, H, hk, hd, cap, starts, lens, dt)
     want = oracle.decode_attention(q, k, v, st, ln)
     got = run_gpu(ane, q, k, v, st, ln, dt)
