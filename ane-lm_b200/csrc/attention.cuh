@@ -510,14 +510,16 @@ decode_attention_kernel(const AttnArgs a) {
 
 // ---------------------------------------------------------------------------
 // 16-bit caches: the two contractions on the tensor cores (mma.sync
-// m16n8k16, fp32 accumulation), and a pipelined split.  Rows of the MMA are
-// the kv head's q heads (G <= 8 of 16; the rest are zero), so one warp's
-// scores for 16 keys are two MMA tiles per 16 dims, and P.V for those keys
-// is one 16-deep k-step per 8 dims.  The exps stay in registers and are the
-// A operand of P.V directly (the accumulator layout of the first MMA is the
-// operand layout of the second).  P is split into a high and a low part in
-// the cache's type (fp16 scaled by 2^12 so the low part stays normal), so
-// P.V keeps about 16 (bf16) / 22 (fp16) significant bits of each weight.
+// m16n8k16, fp32 accumulation), and a pipelined split.  Both are taken
+// transposed so that the 16 rows of an MMA tile are all used: S^T = K Q^T
+// has a warp's 16 keys as rows and the kv head's q heads as the 8 columns
+// (G <= 8; the rest are zero), one MMA per 16 dims; O^T = V^T P^T has 16
+// dims as rows, one MMA per 16 dims and part of P.  The exps stay in
+// registers: movmatrix transposes them from the accumulator layout of the
+// first product into the operand layout of the second.  P is split into a
+// high and a low part in the cache's type (fp16 scaled by 2^12 so the low
+// part stays normal), so P.V keeps about 16 (bf16) / 22 (fp16) significant
+// bits of each weight.
 //
 // A CTA takes `chunks` consecutive 64-key chunks of one (kv head,
 // sequence); warp w takes keys 16w .. 16w+15 of every chunk.  Each warp
@@ -536,22 +538,35 @@ decode_attention_kernel(const AttnArgs a) {
 // fp32 kernel's (the MMA's internal order is the hardware's): results
 // agree with the fp32 order to within the output type's rounding.
 // K and V rows sit in shared memory with a 16-byte pad per row, which makes
-// the fragment loads (32-bit loads for K, ldmatrix.trans for V) free of bank
+// the fragment loads (ldmatrix for K, ldmatrix.trans for V) free of bank
 // conflicts.
 template <typename T>
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0,
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
-    const uint32_t z = 0u;  // rows 8-15 of A: no heads there
     if constexpr (std::is_same<T, F16>::value)
         asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
                      "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-                     : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
     else
         asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
                      "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
                      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-                     : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+                     : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+// transposes an 8x8 matrix of 16-bit values held one pair per lane (row
+// lane / 4, columns 2 (lane % 4) and + 1)
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t v) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(v));
+    return d;
 }
 
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
@@ -682,26 +697,33 @@ decode_attention_mma_kernel(const AttnArgs a) {
     };
     for (int j = 0; j < ns; j++) issue(j, j);
 
-    // q fragments (rows = heads gid < G; others zero), loaded while the copies fly
-    uint32_t qa[KSTEPS][2];
+    // q fragments: the B operand of S^T = K Q^T (column gid = head gid < G;
+    // other columns zero), loaded while the copies fly
+    uint32_t qb[KSTEPS][2];
     {
         const bool hv = gid < G;
         const S* qp = static_cast<const S*>(a.q) + b * a.q_stride +
                       (int64_t)(h0 + (hv ? gid : 0)) * a.q_head_stride + 2 * tq;
 #pragma unroll
         for (int ks = 0; ks < KSTEPS; ks++) {
-            qa[ks][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qp + 16 * ks)) : 0u;
-            qa[ks][1] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qp + 16 * ks + 8)) : 0u;
+            qb[ks][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qp + 16 * ks)) : 0u;
+            qb[ks][1] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qp + 16 * ks + 8)) : 0u;
         }
     }
 
     // ---- 2. the chunks: scores, online softmax, P.V --------------------------
-    // this thread: head gid, keys k0 + {0, 1, 8, 9} of the warp's 16
-    const int k0 = 2 * tq;
-    float o[HD / 8][4];  // rows gid (elements 0, 1); rows gid + 8 stay zero
+    // Transposed products fill the 16-row MMA tiles: S^T = K Q^T (rows: the
+    // warp's 16 keys) and O^T = V^T P^T (rows: 16 dims), with P^T moved from
+    // the accumulator layout of the first to the operand layout of the
+    // second by movmatrix.  This thread: keys gid and gid + 8, heads
+    // hA = 2 tq and hB = 2 tq + 1.
+    const int mi = lane >> 3, rr = lane & 7;  // ldmatrix: matrix, row
+    const int koffK = ((mi & 1) * 8 + rr) * RS + (mi >> 1) * 8;  // keys (mi&1)*8+rr, dims +0/+8
+    const int koffV = ((mi >> 1) * 8 + rr) * RS + (mi & 1) * 8;  // keys (mi>>1)*8+rr, dims +0/+8
+    float o[HD / 16][4];  // O^T: dims 16t + gid (+8) x heads hA, hB
 #pragma unroll
-    for (int nb = 0; nb < HD / 8; nb++) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;
+    for (int t = 0; t < HD / 16; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.0f;
+    float mA = -INFINITY, mB = -INFINITY, lA = 0.0f, lB = 0.0f;
     int st = 0;
     for (int j = 0; j < nc; j++) {
         cp_async_wait_pending(ns - 1);  // chunk j's group has landed (this lane's copies)
@@ -711,84 +733,86 @@ decode_attention_mma_kernel(const AttnArgs a) {
         if (nw > 0) {
             const S* const sK = ring + st * STAGE;
             const S* const sV = sK + WK * RS;
-            float sc[2][4];
+            float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int nb = 0; nb < 2; nb++) {
-                sc[nb][0] = sc[nb][1] = sc[nb][2] = sc[nb][3] = 0.0f;
-                const S* kr = sK + (8 * nb + gid) * RS + k0;
-#pragma unroll
-                for (int ks = 0; ks < KSTEPS; ks++) {
-                    const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks);
-                    const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + 16 * ks + 8);
-                    mma16816<T>(sc[nb], qa[ks][0], qa[ks][1], b0, b1);
-                }
+            for (int ks = 0; ks < KSTEPS; ks++) {
+                uint32_t ka[4];
+                ldsm_x4(ka, sK + koffK + 16 * ks);
+                mma16816<T>(sc, ka, qb[ks][0], qb[ks][1]);
             }
             // rows past the keys hold stale data: their scores become -inf
             // by selection, and their V fragments are zeroed below
-            float x[4] = {sc[0][0], sc[0][1], sc[1][0], sc[1][1]};
-            const int koff[4] = {0, 1, 8, 9};
-            float cm = -INFINITY;
+            const bool v0 = gid < nw, v1 = gid + 8 < nw;
+            const float x0 = v0 ? __fmul_rn(sc[0], a.scale) : -INFINITY;  // key gid, hA
+            const float x1 = v0 ? __fmul_rn(sc[1], a.scale) : -INFINITY;  // key gid, hB
+            const float x2 = v1 ? __fmul_rn(sc[2], a.scale) : -INFINITY;  // key gid + 8, hA
+            const float x3 = v1 ? __fmul_rn(sc[3], a.scale) : -INFINITY;  // key gid + 8, hB
+            float cA = fmaxf(x0, x2), cB = fmaxf(x1, x3);
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                x[i] = k0 + koff[i] < nw ? __fmul_rn(x[i], a.scale) : -INFINITY;
-                cm = fmaxf(cm, x[i]);
+            for (int off = 4; off <= 16; off <<= 1) {  // over the 8 key rows (gid)
+                cA = fmaxf(cA, __shfl_xor_sync(0xffffffffu, cA, off));
+                cB = fmaxf(cB, __shfl_xor_sync(0xffffffffu, cB, off));
             }
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 1));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 2));
-            const float m_new = fmaxf(m_run, cm);
-            float e[4];
-            {
-                const float2 d01 = make_float2(__fsub_rn(x[0], m_new), __fsub_rn(x[1], m_new));
-                const float2 d23 = make_float2(__fsub_rn(x[2], m_new), __fsub_rn(x[3], m_new));
-                const float2 e01 = pinned_expf_nonpos2(d01), e23 = pinned_expf_nonpos2(d23);
-                // NaN scores stay NaN, as in pinned_expf
-                e[0] = d01.x != d01.x ? d01.x : e01.x;
-                e[1] = d01.y != d01.y ? d01.y : e01.y;
-                e[2] = d23.x != d23.x ? d23.x : e23.x;
-                e[3] = d23.y != d23.y ? d23.y : e23.y;
-            }
-            const float f = pinned_expf(__fsub_rn(m_run, m_new));  // 0 on the first keys
-            l_run = __fmaf_rn(l_run, f, __fadd_rn(__fadd_rn(e[0], e[1]), __fadd_rn(e[2], e[3])));
-            if (__any_sync(0xffffffffu, m_new != m_run)) {
+            const float nA = fmaxf(mA, cA), nB = fmaxf(mB, cB);
+            // exps of x - m (<= 0, or NaN); NaN arguments stay NaN, as in pinned_expf
+            auto exp2v = [](float2 d) {
+                const float2 e = pinned_expf_nonpos2(d);
+                return make_float2(d.x != d.x ? d.x : e.x, d.y != d.y ? d.y : e.y);
+            };
+            const float2 e01 = exp2v(make_float2(__fsub_rn(x0, nA), __fsub_rn(x1, nB)));
+            const float2 e23 = exp2v(make_float2(__fsub_rn(x2, nA), __fsub_rn(x3, nB)));
+            const float2 f = exp2v(make_float2(__fsub_rn(mA, nA), __fsub_rn(mB, nB)));  // 0 at first
+            lA = __fmaf_rn(lA, f.x, __fadd_rn(e01.x, e23.x));
+            lB = __fmaf_rn(lB, f.y, __fadd_rn(e01.y, e23.y));
+            if (__any_sync(0xffffffffu, nA != mA || nB != mB)) {
 #pragma unroll
-                for (int nb = 0; nb < HD / 8; nb++) {
-                    o[nb][0] = __fmul_rn(o[nb][0], f);
-                    o[nb][1] = __fmul_rn(o[nb][1], f);
+                for (int t = 0; t < HD / 16; t++) {
+                    o[t][0] = __fmul_rn(o[t][0], f.x);
+                    o[t][1] = __fmul_rn(o[t][1], f.y);
+                    o[t][2] = __fmul_rn(o[t][2], f.x);
+                    o[t][3] = __fmul_rn(o[t][3], f.y);
                 }
             }
-            m_run = m_new;
-            // P as the A operand of P.V: high and low parts
-            uint32_t ph[2], pl[2];
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const float p0 = __fmul_rn(e[2 * h], PSCALE), p1 = __fmul_rn(e[2 * h + 1], PSCALE);
-                ph[h] = pack2<T>(p0, p1);
-                pl[h] = pack2<T>(__fsub_rn(p0, low_f<T>(ph[h])), __fsub_rn(p1, high_f<T>(ph[h])));
+            mA = nA;
+            mB = nB;
+            // P^T (keys x heads) in high and low parts, then transposed into
+            // the B operand of O^T = V^T P^T: column gid = head gid, rows =
+            // keys 2 tq, 2 tq + 1 (+ 8)
+            uint32_t bh[2], bl[2];
+            {
+                const float p0 = __fmul_rn(e01.x, PSCALE), p1 = __fmul_rn(e01.y, PSCALE);
+                const float p2 = __fmul_rn(e23.x, PSCALE), p3 = __fmul_rn(e23.y, PSCALE);
+                const uint32_t h01 = pack2<T>(p0, p1), h23 = pack2<T>(p2, p3);
+                const uint32_t l01 = pack2<T>(__fsub_rn(p0, low_f<T>(h01)), __fsub_rn(p1, high_f<T>(h01)));
+                const uint32_t l23 = pack2<T>(__fsub_rn(p2, low_f<T>(h23)), __fsub_rn(p3, high_f<T>(h23)));
+                bh[0] = movmatrix_trans(h01);
+                bh[1] = movmatrix_trans(h23);
+                bl[0] = movmatrix_trans(l01);
+                bl[1] = movmatrix_trans(l23);
             }
-            // ldmatrix.trans gives this thread V[keys kh*8 + k0, +1][dim]:
-            // halves of keys >= nw are zeroed (their weight is 0, the data stale)
-            const int mi = lane >> 3, rr = lane & 7;
-            const S* vb = sV + ((mi & 1) * 8 + rr) * RS + (mi >> 1) * 8;
+            // V^T fragments by ldmatrix.trans: this thread gets
+            // V[keys 2tq, 2tq+1 (+8)][dim]; halves of keys >= nw are zeroed
+            // (their weight is 0, the data stale)
+            const S* const vb = sV + koffV;
             auto pv = [&](auto masked) {
                 uint32_t vm0 = 0xffffffffu, vm1 = 0xffffffffu;
                 if constexpr (decltype(masked)::value) {
+                    const int k0 = 2 * tq;
                     vm0 = (k0 < nw ? 0x0000ffffu : 0u) | (k0 + 1 < nw ? 0xffff0000u : 0u);
                     vm1 = (k0 + 8 < nw ? 0x0000ffffu : 0u) | (k0 + 9 < nw ? 0xffff0000u : 0u);
                 }
 #pragma unroll
-                for (int d0 = 0; d0 < HD; d0 += 16) {
-                    uint32_t r[4];
-                    ldsm_x4_trans(r, vb + d0);
+                for (int t = 0; t < HD / 16; t++) {
+                    uint32_t va[4];
+                    ldsm_x4_trans(va, vb + 16 * t);
                     if constexpr (decltype(masked)::value) {
-                        r[0] &= vm0;
-                        r[1] &= vm1;
-                        r[2] &= vm0;
-                        r[3] &= vm1;
+                        va[0] &= vm0;
+                        va[1] &= vm0;
+                        va[2] &= vm1;
+                        va[3] &= vm1;
                     }
-                    mma16816<T>(o[d0 / 8], ph[0], ph[1], r[0], r[1]);
-                    mma16816<T>(o[d0 / 8], pl[0], pl[1], r[0], r[1]);
-                    mma16816<T>(o[d0 / 8 + 1], ph[0], ph[1], r[2], r[3]);
-                    mma16816<T>(o[d0 / 8 + 1], pl[0], pl[1], r[2], r[3]);
+                    mma16816<T>(o[t], va, bh[0], bh[1]);
+                    mma16816<T>(o[t], va, bl[0], bl[1]);
                 }
             };
             if (nw == WK)
@@ -802,24 +826,46 @@ decode_attention_mma_kernel(const AttnArgs a) {
     }
 
     // ---- 3. merge the four warps into the split's (M, L, O) -------------------
-    l_run = __fadd_rn(l_run, __shfl_xor_sync(0xffffffffu, l_run, 1));
-    l_run = __fadd_rn(l_run, __shfl_xor_sync(0xffffffffu, l_run, 2));
-    if (tq == 0 && gid < G) {
-        s_wm[gid][w] = m_run;
-        s_wl[gid][w] = l_run;
-    }
-    // after this barrier the rings are dead (every chunk's copies were waited for)
-    __syncthreads();
-    if (gid < G) {
-        const float M = fmaxf(fmaxf(s_wm[gid][0], s_wm[gid][1]), fmaxf(s_wm[gid][2], s_wm[gid][3]));
-        const float fw = __fmul_rn(pinned_expf(__fsub_rn(m_run, M)), 1.0f / PSCALE);
 #pragma unroll
-        for (int nb = 0; nb < HD / 8; nb++)
-            *reinterpret_cast<float2*>(s_red + (w * G + gid) * HD + 8 * nb + k0) =
-                make_float2(__fmul_rn(o[nb][0], fw), __fmul_rn(o[nb][1], fw));
+    for (int off = 4; off <= 16; off <<= 1) {
+        lA = __fadd_rn(lA, __shfl_xor_sync(0xffffffffu, lA, off));
+        lB = __fadd_rn(lB, __shfl_xor_sync(0xffffffffu, lB, off));
+    }
+    const int hA = 2 * tq, hB = 2 * tq + 1;
+    if (gid == 0) {
+        if (hA < G) {
+            s_wm[hA][w] = mA;
+            s_wl[hA][w] = lA;
+        }
+        if (hB < G) {
+            s_wm[hB][w] = mB;
+            s_wl[hB][w] = lB;
+        }
+    }
+    __syncthreads();  // the rings are dead: every chunk's copies were waited for
+    auto wmax = [&](int h) {
+        return fmaxf(fmaxf(s_wm[h][0], s_wm[h][1]), fmaxf(s_wm[h][2], s_wm[h][3]));
+    };
+    if (hA < G) {
+        const float fw = __fmul_rn(pinned_expf(__fsub_rn(mA, wmax(hA))), 1.0f / PSCALE);
+        float* const r = s_red + (w * G + hA) * HD + gid;
+#pragma unroll
+        for (int t = 0; t < HD / 16; t++) {
+            r[16 * t] = __fmul_rn(o[t][0], fw);
+            r[16 * t + 8] = __fmul_rn(o[t][2], fw);
+        }
+    }
+    if (hB < G) {
+        const float fw = __fmul_rn(pinned_expf(__fsub_rn(mB, wmax(hB))), 1.0f / PSCALE);
+        float* const r = s_red + (w * G + hB) * HD + gid;
+#pragma unroll
+        for (int t = 0; t < HD / 16; t++) {
+            r[16 * t] = __fmul_rn(o[t][1], fw);
+            r[16 * t + 8] = __fmul_rn(o[t][3], fw);
+        }
     }
     if (tid < G) {
-        const float M = fmaxf(fmaxf(s_wm[tid][0], s_wm[tid][1]), fmaxf(s_wm[tid][2], s_wm[tid][3]));
+        const float M = wmax(tid);
         float lw[kAttnWarps];
 #pragma unroll
         for (int v = 0; v < kAttnWarps; v++)
