@@ -900,27 +900,43 @@ int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
         constexpr int smax = attn_mma_max_stages<HD>();
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)attn_mma_smem_bytes<HD>(smax));
-        // CTAs resident per SM with full rings (the same on every device of
-        // a process: one query)
-        static std::atomic<int> occ{0};
-        int per_sm = occ.load(std::memory_order_relaxed);
-        if (e == cudaSuccess && per_sm == 0) {
+        // CTAs resident per SM with rings of 1 .. smax stages (the same on
+        // every device of a process: queried once)
+        static std::atomic<int> occ[kAttnMaxStages + 1];
+        for (int st = 1; st <= smax && e == cudaSuccess; st++) {
+            if (occ[st].load(std::memory_order_relaxed) > 0) continue;
+            int per_sm = 0;
             e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kAttnThreads,
-                                                              attn_mma_smem_bytes<HD>(smax));
-            if (per_sm < 1) per_sm = 1;
-            occ.store(per_sm, std::memory_order_relaxed);
+                                                              attn_mma_smem_bytes<HD>(st));
+            occ[st].store(per_sm < 1 ? 1 : per_sm, std::memory_order_relaxed);
         }
         if (e != cudaSuccess)
             return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
         // Split each (kv head, sequence) into just enough CTAs to fill the
         // resident slots once: long splits keep the copy rings busy and
-        // leave few partials to merge.
+        // leave few partials to merge.  The slots depend on the ring depth,
+        // which follows the chunks per CTA (up to smax), so each depth is
+        // tried and the choice that needs exactly that depth and gives the
+        // most CTAs is kept (one chunk per CTA and one stage at batch 1,
+        // a single split and smax stages at large batch).
         const int nchunk = a.max_splits;  // 64-key chunks of the longest sequence
-        const int64_t pairs = batch * a.n_kv, slots = (int64_t)sm_count() * per_sm;
-        int64_t nsplit = pairs >= slots ? 1 : slots / pairs;
-        if (nsplit > nchunk) nsplit = nchunk;
-        la.chunks = (int)((nchunk + nsplit - 1) / nsplit);
-        la.stages = la.chunks < smax ? la.chunks : smax;
+        const int64_t pairs = batch * a.n_kv;
+        int64_t best_ctas = 0;
+        la.chunks = nchunk;
+        la.stages = smax < nchunk ? smax : nchunk;
+        for (int st = 1; st <= smax; st++) {
+            const int64_t slots = (int64_t)sm_count() * occ[st].load(std::memory_order_relaxed);
+            int64_t nsplit = pairs >= slots ? 1 : slots / pairs;
+            if (nsplit > nchunk) nsplit = nchunk;
+            const int chunks = (int)((nchunk + nsplit - 1) / nsplit);
+            const int need = chunks < smax ? chunks : smax;
+            const int64_t ctas = pairs * ((nchunk + chunks - 1) / chunks);
+            if (need == st && ctas > best_ctas) {
+                best_ctas = ctas;
+                la.chunks = chunks;
+                la.stages = st;
+            }
+        }
         gx = (unsigned)((nchunk + la.chunks - 1) / la.chunks);
         smem = attn_mma_smem_bytes<HD>(la.stages);
     } else {
