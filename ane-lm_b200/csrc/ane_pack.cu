@@ -79,6 +79,29 @@ __device__ __forceinline__ uint32_t f2h(float x) {
     else return f2h_rne(x);
 }
 
+// two values -> a packed pair of f16 bits (a in the low half), by one
+// paired hardware conversion.  Round to nearest: NaNs then replaced as in
+// f2h_rne.  Truncating: round-toward-zero conversion is f2h_trunc's
+// truncation, subnormals included, except where f2h_trunc saturates
+// (|x| >= 65536, Inf and NaN -> signed Inf), replaced after.
+template <bool TRUNC>
+__device__ __forceinline__ uint32_t f2h_pair(float a, float b) {
+    if constexpr (TRUNC) {
+        uint32_t h;
+        asm("cvt.rz.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));  // b -> high half
+        const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+        if ((ua & 0x7FFFFFFFu) >= 0x47800000u) h = (h & 0xFFFF0000u) | ((ua >> 16) & 0x8000u) | 0x7C00u;
+        if ((ub & 0x7FFFFFFFu) >= 0x47800000u) h = (h & 0x0000FFFFu) | (ub & 0x80000000u) | 0x7C000000u;
+        return h;
+    } else {
+        const __half2 hh = __floats2half2_rn(a, b);
+        uint32_t h = *reinterpret_cast<const uint32_t*>(&hh);
+        if (a != a) h = (h & 0xFFFF0000u) | ((__float_as_uint(a) >> 16) & 0x8000u) | 0x7E00u;
+        if (b != b) h = (h & 0x0000FFFFu) | ((__float_as_uint(b) & 0x80000000u) | 0x7E000000u);
+        return h;
+    }
+}
+
 // in [tokens][in_stride] f32 -> surface [ceil(tokens/32)][channels][32] f16.
 template <bool TRUNC, bool VEC>
 __global__ void __launch_bounds__(kPackThreads)
@@ -91,14 +114,25 @@ ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, in
     const int64_t t0 = s * kSpatial;
     const int nt = (int)min((int64_t)kSpatial, tokens - t0);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    // token rows -> tile[t][c]
-    for (int r = w; r < nt; r += kPackThreads / kWarp) {
-        const float* row = in + (t0 + r) * in_stride + c0;
-        if (VEC && nc == kPackCh) {
-            const float4 v = __ldcs(reinterpret_cast<const float4*>(row) + lane);
-            *reinterpret_cast<float4*>(tile + tslot(r, 4 * lane)) = v;
-        } else {
-            for (int c = lane; c < nc; c += kWarp) tile[tslot(r, c)] = __ldcs(row + c);
+    // token rows -> tile[t][c]; a full tile's four rows per warp are all
+    // loaded before any is stored, so they are in flight together
+    constexpr int RPW = kSpatial / (kPackThreads / kWarp);  // rows per warp
+    if (VEC && nc == kPackCh && nt == kSpatial) {
+        float4 v[RPW];
+#pragma unroll
+        for (int k = 0; k < RPW; k++)
+            v[k] = __ldcs(reinterpret_cast<const float4*>(in + (t0 + w + 8 * k) * in_stride + c0) + lane);
+#pragma unroll
+        for (int k = 0; k < RPW; k++) *reinterpret_cast<float4*>(tile + tslot(w + 8 * k, 4 * lane)) = v[k];
+    } else {
+        for (int r = w; r < nt; r += kPackThreads / kWarp) {
+            const float* row = in + (t0 + r) * in_stride + c0;
+            if (VEC && nc == kPackCh) {
+                const float4 v = __ldcs(reinterpret_cast<const float4*>(row) + lane);
+                *reinterpret_cast<float4*>(tile + tslot(r, 4 * lane)) = v;
+            } else {
+                for (int c = lane; c < nc; c += kWarp) tile[tslot(r, c)] = __ldcs(row + c);
+            }
         }
     }
     __syncthreads();
@@ -109,15 +143,10 @@ ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, in
         uint16_t* dst = sbase + c * kSpatial + 8 * q;
         const float* col = tile + tslot(8 * q, c);  // tokens 8q .. 8q+7 share the swizzle
         if (nt == kSpatial) {
-            uint32_t h[8];
+            uint32_t h[4];
 #pragma unroll
-            for (int i = 0; i < 8; i++) h[i] = f2h<TRUNC>(col[i * kPackCh]);
-            uint4 v;
-            v.x = h[0] | (h[1] << 16);
-            v.y = h[2] | (h[3] << 16);
-            v.z = h[4] | (h[5] << 16);
-            v.w = h[6] | (h[7] << 16);
-            __stcs(reinterpret_cast<uint4*>(dst), v);
+            for (int i = 0; i < 4; i++) h[i] = f2h_pair<TRUNC>(col[2 * i * kPackCh], col[(2 * i + 1) * kPackCh]);
+            __stcs(reinterpret_cast<uint4*>(dst), make_uint4(h[0], h[1], h[2], h[3]));
         } else {
             for (int i = 0; i < 8 && 8 * q + i < nt; i++)
                 dst[i] = (uint16_t)f2h<TRUNC>(col[i * kPackCh]);
@@ -138,14 +167,28 @@ ane_unpack_kernel(float* __restrict__ out, int64_t out_stride, const uint16_t* _
     const int nt = (int)min((int64_t)kSpatial, tokens - t0);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const uint16_t* const sbase = surface + (s * channels + c0) * kSpatial;
-    for (int item = tid; item < nc * 4; item += kPackThreads) {
+    auto put = [&](int item, const uint4 v) {  // 8 slots of a channel -> the tile
         const int c = item >> 2, q = item & 3;
-        if (8 * q >= nt) continue;
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(sbase + c * kSpatial + 8 * q));
         const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
         float* col = tile + tslot(8 * q, c);  // tokens 8q .. 8q+7 share the swizzle
 #pragma unroll
         for (int i = 0; i < 8; i++) col[i * kPackCh] = h2f_fast((wd[i >> 1] >> (16 * (i & 1))) & 0xFFFFu);
+    };
+    constexpr int IPT = kPackCh * 4 / kPackThreads;  // items per thread of a full tile
+    if (nc == kPackCh && nt == kSpatial) {
+        uint4 v[IPT];  // all loaded before any is converted
+#pragma unroll
+        for (int k = 0; k < IPT; k++) {
+            const int item = tid + k * kPackThreads;
+            v[k] = __ldcs(reinterpret_cast<const uint4*>(sbase + (item >> 2) * kSpatial + 8 * (item & 3)));
+        }
+#pragma unroll
+        for (int k = 0; k < IPT; k++) put(tid + k * kPackThreads, v[k]);
+    } else {
+        for (int item = tid; item < nc * 4; item += kPackThreads) {
+            if (8 * (item & 3) >= nt) continue;
+            put(item, __ldcs(reinterpret_cast<const uint4*>(sbase + (item >> 2) * kSpatial + 8 * (item & 3))));
+        }
     }
     __syncthreads();
     for (int r = w; r < nt; r += kPackThreads / kWarp) {

@@ -19,7 +19,8 @@ def values(rng, shape):
     k = max(1, n // 50)
     idx = rng.choice(n, size=min(n, 8 * k), replace=False)
     specials = np.array([np.inf, -np.inf, np.nan, -np.nan, 0.0, -0.0, 65504.0, 65519.99, 65520.0,
-                         1e6, -1e6, 6.1e-5, 5.96e-8, 2.98e-8, 2.99e-8, 1e-10, -3e-7], np.float32)
+                         1e6, -1e6, 6.1e-5, 5.96e-8, 2.98e-8, 2.99e-8, 1e-10, -3e-7,
+                         65536.0, -65536.0, 65535.996, -65535.996, 3.4e38], np.float32)
     flat[idx[:k]] = rng.choice(specials, k)
     flat[idx[k:2 * k]] = rng.standard_normal(k).astype(np.float32) * np.float32(1e-5)  # subnormal range
     flat[idx[2 * k:3 * k]] = (rng.integers(0, 1 << 32, k, dtype=np.uint64).astype(np.uint32)).view(np.float32)
