@@ -5,8 +5,9 @@
 //   SILU        x   =  x / (1 + exp(-x))                 silu_vec_inplace
 //   MUL_SIGMOID y   =  y / (1 + exp(-z))                 mul_sigmoid_inplace
 //
-// Element-wise and HBM-bound: 16-byte vectors, evict-first accesses, a grid
-// sized to the SM count.  fp32 rows use the pinned Cody-Waite/Taylor exp and
+// Element-wise and HBM-bound: long contiguous inputs stream through a
+// bulk-copy ring in shared memory (act_bulk_kernel); the rest use 16-byte
+// vectors with evict-first accesses and a grid sized to the SM count.  fp32 rows use the pinned Cody-Waite/Taylor exp and
 // an IEEE divide, each step rounded on its own, as the reference's vneg /
 // vvexpf / vsadd / vdiv sequence (bit-exact).  fp16 / bf16 rows use the
 // special-function unit's exp2 and reciprocal: the pinned form costs about
@@ -118,6 +119,85 @@ act_vec_kernel(const ActArgs p) {
     }
 }
 
+
+// Long contiguous inputs: a persistent CTA per SM streams 32 KB tiles of
+// each input through a two-stage ring in shared memory, filled by one bulk
+// copy (TMA) per input and tile, while the previous tile is computed from
+// shared memory and stored with 16-byte streaming stores.  Few, large
+// copies keep the DRAM request stream long and sequential; measured on the
+// Qwen3-8B shapes this reaches the copy roofline where the grid-stride
+// 16-byte loads above stop about 10% short.  Results are the same
+// element-wise functions, so the same bits.
+constexpr int kBulkTile = 32768;  // bytes per input per tile
+constexpr int kBulkStages = 2;
+template <int NIN>
+constexpr size_t act_bulk_smem() { return (size_t)kBulkStages * NIN * kBulkTile; }
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kActThreads)
+act_bulk_kernel(const ActArgs p, int64_t ntiles, unsigned int* flags) {
+    using S = typename T::storage;
+    constexpr int V = T::kVec;
+    constexpr int NIN = MODE == SILU ? 1 : 2;
+    constexpr int STEPS = kBulkTile / (kActThreads * 16);  // 16-byte vectors per thread and tile
+    extern __shared__ __align__(128) unsigned char smem[];  // [stage][input][kBulkTile]
+    __shared__ __align__(8) uint64_t full[kBulkStages];
+    const int tid = threadIdx.x;
+    const int64_t G = gridDim.x;
+    const char* const src0 = static_cast<const char*>(p.a);
+    const char* const src1 = static_cast<const char*>(p.b);
+    char* const dst = static_cast<char*>(p.out);
+    if (tid == 0) {
+        for (int s = 0; s < kBulkStages; s++) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    // thread 0: tile -> stage s.  The stage was last read through the
+    // generic proxy (before the barrier that precedes the call); the proxy
+    // fence orders those reads before the copy's writes.
+    auto issue = [&](int64_t tile, int s) {
+        fence_proxy_async();
+        mbar_expect_tx(&full[s], NIN * kBulkTile);
+        bulk_load(smem + (s * NIN) * kBulkTile, src0 + tile * kBulkTile, kBulkTile, &full[s]);
+        if constexpr (NIN == 2)
+            bulk_load(smem + (s * NIN + 1) * kBulkTile, src1 + tile * kBulkTile, kBulkTile, &full[s]);
+    };
+    if (tid == 0)
+        for (int s = 0; s < kBulkStages; s++)
+            if (blockIdx.x + s * G < ntiles) issue(blockIdx.x + s * G, s);
+    int s = 0;
+    uint32_t ph = 0u;
+    for (int64_t tile = blockIdx.x; tile < ntiles; tile += G) {
+        if (!__syncthreads_and(mbar_wait_bounded(&full[s], (ph >> s) & 1u))) {
+            // a copy did not land in time: flag it, wait (bounded) once more
+            // for every stage still in flight, and stop
+            if (tid == 0) {
+                if (flags) atomicOr(flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+                for (int k = 0; k < kBulkStages; k++) {
+                    const int sk = (s + k) % kBulkStages;
+                    if (tile + k * G < ntiles) mbar_wait_bounded(&full[sk], (ph >> sk) & 1u);
+                }
+            }
+            return;
+        }
+        ph ^= 1u << s;
+        const unsigned char* const in0 = smem + (s * NIN) * kBulkTile;
+#pragma unroll
+        for (int st = 0; st < STEPS; st++) {
+            const int off = (st * kActThreads + tid) * 16;
+            float x[V], y[V];
+            unpack<T>(*reinterpret_cast<const uint4*>(in0 + off), x);
+            if constexpr (NIN == 2) unpack<T>(*reinterpret_cast<const uint4*>(in0 + kBulkTile + off), y);
+#pragma unroll
+            for (int e = 0; e < V; e++) x[e] = act<T, MODE>(x[e], NIN == 2 ? y[e] : 0.0f);
+            st_stream(reinterpret_cast<S*>(dst + tile * kBulkTile + off), pack<T>(x));
+        }
+        __syncthreads();  // stage s consumed by every thread
+        if (tid == 0 && tile + kBulkStages * G < ntiles) issue(tile + kBulkStages * G, s);
+        s = s + 1 == kBulkStages ? 0 : s + 1;
+    }
+}
+
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kActThreads)
 act_scalar_kernel(const ActArgs p) {
@@ -144,6 +224,32 @@ static int launch_act(ActArgs p, cudaStream_t s) {
         p.n *= p.rows;
         p.out_stride = p.a_stride = p.b_stride = p.n;
         p.rows = 1;
+    }
+    // long contiguous inputs: the bulk-copy ring over whole tiles, the
+    // remainder (less than a tile) by the kernels below
+    if (vec && p.rows == 1) {
+        const int64_t ntiles = p.n * es / kBulkTile;
+        if (ntiles >= 2 * (int64_t)sm_count()) {
+            constexpr int nin = MODE == SILU ? 1 : 2;
+            const void* kb = reinterpret_cast<const void*>(act_bulk_kernel<T, MODE>);
+            const cudaError_t e = cudaFuncSetAttribute(act_bulk_kernel<T, MODE>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       (int)act_bulk_smem<nin>());
+            if (e != cudaSuccess) return fail(ANE_CUDA_ERR_CUDA, "activation: %s", cudaGetErrorString(e));
+            const int blocks = resident_grid(kb, kActThreads, act_bulk_smem<nin>(), ntiles);
+            act_bulk_kernel<T, MODE><<<blocks, kActThreads, act_bulk_smem<nin>(), s>>>(p, ntiles, status_flags_device());
+            const int64_t done = ntiles * (kBulkTile / es);
+            if (done == p.n) return check_launch("activation");
+            const int st = check_launch("activation");
+            if (st) return st;
+            ActArgs t = p;
+            t.out = static_cast<char*>(p.out) + done * es;
+            t.a = static_cast<const char*>(p.a) + done * es;
+            if (p.b) t.b = static_cast<const char*>(p.b) + done * es;
+            t.n = p.n - done;
+            t.out_stride = t.a_stride = t.b_stride = t.n;
+            return launch_act<T, MODE>(t, s);
+        }
     }
     const int64_t items = vec ? p.rows * (p.n / V) : p.rows * p.n;
     const int64_t want = (items + kActUnroll * kActThreads - 1) / (kActUnroll * kActThreads);

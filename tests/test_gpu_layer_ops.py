@@ -164,6 +164,53 @@ def test_silu_mul(ane, oracle, dt, shape):
         assert ulp(got, want, dt).max() <= 1
 
 
+# Long contiguous inputs take the bulk-copy ring (whole 32 KB tiles) and
+# the plain kernel for the remainder: 701 x 12288 elements end mid-tile.
+@pytest.mark.parametrize("dt", ["f16", "f32", "bf16"])
+def test_silu_mul_bulk_path(ane, oracle, dt):
+    rng = np.random.default_rng(701)
+    shape = (701, 12288)
+    g = rand(rng, shape, dt, scale=3.0, outliers=0.01)
+    u = rand(rng, shape, dt)
+    got = to_host(ane.silu_mul(to_dev(g, dt), to_dev(u, dt)), dt)
+    want = oracle.silu_mul(g, u)
+    if dt == "f32":
+        assert np.array_equal(got.view(np.int32), want.view(np.int32))
+    else:
+        assert ulp(got, want, dt).max() <= 1
+
+
+@pytest.mark.parametrize("dt", ["f16", "f32", "bf16"])
+@pytest.mark.parametrize("op", ["silu_inplace", "mul_sigmoid_inplace"])
+def test_inplace_bulk_matches_pieces(ane, dt, op):
+    """The in-place forms on one long array (bulk-copy ring) give the bits of
+    the same call on pieces too short for it (the 16-byte-vector kernel)."""
+    torch = _torch()
+    rng = np.random.default_rng(17)
+    n = 701 * 12288
+    x = rand(rng, (1, n), dt, scale=3.0, outliers=0.01)
+    z = rand(rng, (1, n), dt, scale=3.0)
+    code = {"f32": 0, "f16": 1, "bf16": 2}[dt]
+    fn = getattr(ane.lib(), "ane_cuda_" + op)
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run(xd, zd, start, count):
+        es = xd.element_size()
+        px, pz = xd.data_ptr() + start * es, zd.data_ptr() + start * es
+        st = fn(code, px, count, s) if op == "silu_inplace" else fn(code, px, pz, count, s)
+        assert st == 0
+
+    whole, zd = to_dev(x, dt), to_dev(z, dt)
+    run(whole, zd, 0, n)
+    pieces = to_dev(x, dt)
+    step = n // 64 + 8  # pieces well below the bulk threshold, ragged last one
+    for start in range(0, n, step):
+        run(pieces, zd, start, min(step, n - start))
+    torch.cuda.synchronize()
+    a, b = to_host(whole, dt), to_host(pieces, dt)
+    assert np.array_equal(a.view(np.uint8), b.view(np.uint8))
+
+
 def test_silu_extremes(ane, oracle):
     g = np.array([[0.0, -0.0, -100.0, 100.0, -88.0, 88.0, -250.0, 250.0, 1e-30, -1e-30,
                    60000.0, -60000.0, 3.0, -3.0, 0.5, -0.5]], np.float32)
