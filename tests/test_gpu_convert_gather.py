@@ -24,7 +24,10 @@ def test_convert_exhaustive_golden(ane):
 
 
 @pytest.mark.parametrize("n,offset", [(1, 0), (7, 0), (8, 0), (1000003, 0), (4096, 1),
-                                      (65541, 3), (1 << 20, 0)])
+                                      (65541, 3), (1 << 20, 0),
+                                      # long enough for the bulk-copy ring, ending mid-tile;
+                                      # 16-byte aligned and unaligned starts
+                                      (10000005, 0), (10000005, 8), (10000005, 3)])
 def test_convert_ragged_and_unaligned(ane, oracle, n, offset):
     torch = _torch()
     rng = np.random.default_rng(n + offset)
