@@ -247,7 +247,10 @@ ANE_CUDA_API int ane_cuda_ane_unpack(float* out, int64_t out_stride, const uint1
  * sets ANE_CUDA_FLAG_BAD_CACHE.  max_len bounds every cache_len[b] and
  * sizes the launch.  fp32 arithmetic; the reference's softmax-weighted sum
  * with its sums taken in a fixed parallel order (within 1e-6 x max|v| of
- * the reference in fp32).
+ * the reference in fp32).  fp16 / bf16 caches: the two products on the
+ * tensor cores with fp32 accumulation and an online softmax; outputs within
+ * one unit of the output type (plus 1e-5 x max|v| near zero) of the
+ * fixed-order fp32 result.
  * head_dim 64, 128 or 256; at most 8 q heads per kv head; q and the caches
  * 16-byte aligned with strides that keep rows 16-byte aligned.
  * Workspace: ane_cuda_decode_attention_workspace_size() bytes (0 when
