@@ -46,7 +46,9 @@ void* g_scratch_addr[kMaxDevices];
 cudaError_t g_scratch_err[kMaxDevices];
 
 // The array's device address on the current device, looked up once per
-// device.
+// device, by the first call made with that device current (the lookup is
+// a runtime call of its own: that first call belongs before any stream
+// capture on the device).
 int static_scratch(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

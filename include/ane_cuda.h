@@ -281,7 +281,9 @@ ANE_CUDA_API int ane_cuda_decode_attention(int dtype, void* out, int64_t out_str
  * Problems needing more scratch than the capacity are rejected
  * (ANE_CUDA_ERR_INVALID_ARG).  The array is shared by all calls on a
  * device: calls whose executions overlap race on it -- order them on one
- * stream. */
+ * stream.  The first call on each device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current); make that first
+ * call before any stream capture on the device. */
 ANE_CUDA_API int64_t ane_cuda_decode_attention_static_capacity(void);
 ANE_CUDA_API int ane_cuda_decode_attention_static(int dtype, void* out, int64_t out_stride,
                                                   const void* q, int64_t q_stride,
