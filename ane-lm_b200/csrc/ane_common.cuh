@@ -69,6 +69,41 @@ __device__ __forceinline__ uint4 ld_keep(const void* p) {
     return __ldg(reinterpret_cast<const uint4*>(p));
 }
 
+// ---------------------------------------------------------------------
+// programmatic dependent launch
+// ---------------------------------------------------------------------
+// The decode-step kernels are launched with programmatic stream
+// serialisation (launch_pdl): the next kernel on the stream may be
+// dispatched while this one drains, which hides most of the launch gap
+// between the short kernels of a decode step.  A kernel so launched calls
+// pdl_begin() before its first global-memory access: griddepcontrol.wait
+// returns once the previous grid on the stream has completed and its
+// writes are visible (immediately when the launch had no such attribute),
+// so ordering and memory visibility are as with a plain launch.  Then
+// launch_dependents lets the next kernel be dispatched; the hardware holds
+// it back until every CTA of this grid has started, so it never takes SM
+// slots this grid still needs.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
 
 // ---------------------------------------------------------------------

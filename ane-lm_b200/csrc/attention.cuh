@@ -317,6 +317,7 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, unsigned char* sm
 template <typename T, int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads)
 decode_attention_kernel(const AttnArgs a) {
+    pdl_begin();
     using S = typename T::storage;
     using Sh = AttnShape<T, HD>;
     constexpr int V = Sh::V, EPL = Sh::EPL, NV = Sh::NV, GL = Sh::GL, KPW = Sh::KPW, U = Sh::U;
@@ -618,6 +619,7 @@ __host__ __device__ constexpr int attn_mma_max_stages() { return HD <= 64 ? 4 : 
 template <typename T, int HD, int G>
 __global__ void __launch_bounds__(kAttnThreads)
 decode_attention_mma_kernel(const AttnArgs a) {
+    pdl_begin();
     using S = typename T::storage;
     static_assert(sizeof(S) == 2, "16-bit caches");
     static_assert(G <= 8, "at most 8 q heads per kv head");
@@ -952,7 +954,7 @@ int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
         }
     }
     const dim3 grid(gx, (unsigned)a.n_kv, (unsigned)batch);
-    kern<<<grid, kAttnThreads, smem, s>>>(la);
+    launch_pdl(kern, grid, kAttnThreads, smem, s, la);
     return check_launch("decode_attention");
 }
 

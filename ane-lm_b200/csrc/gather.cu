@@ -17,6 +17,7 @@ constexpr int kGatherWarps = 4;
 __global__ void __launch_bounds__(kGatherWarps * kWarp)
 gather_vec_kernel(uint4* __restrict__ out, const uint4* __restrict__ table,
                   const int32_t* __restrict__ ids, int64_t rows, int vocab, int64_t row_vec) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kGatherWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -45,6 +46,7 @@ __global__ void __launch_bounds__(kGatherWarps * kWarp)
 gather_elem_kernel(typename TO::storage* __restrict__ out,
                    const typename TI::storage* __restrict__ table,
                    const int32_t* __restrict__ ids, int64_t rows, int vocab, int hidden) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kGatherWarps + (threadIdx.x >> 5);
     if (row >= rows) return;
@@ -108,24 +110,24 @@ int ane_cuda_embedding_gather(void* out, int out_dtype, const void* table, int t
     if (out_dtype == table_dtype) {
         const int64_t row_bytes = (int64_t)hidden * tes;
         if (row_bytes % 16 == 0 && is_aligned(out, 16) && is_aligned(table, 16)) {
-            gather_vec_kernel<<<blocks, kGatherWarps * kWarp, 0, s>>>(
+            launch_pdl(gather_vec_kernel, blocks, kGatherWarps * kWarp, 0, s,
                 reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(table), ids, rows,
                 vocab, row_bytes / 16);
         } else if (table_dtype == ANE_CUDA_F32) {
-            gather_elem_kernel<F32, F32><<<blocks, kGatherWarps * kWarp, 0, s>>>(
+            launch_pdl(gather_elem_kernel<F32, F32>, blocks, kGatherWarps * kWarp, 0, s,
                 (float*)out, (const float*)table, ids, rows, vocab, hidden);
         } else if (table_dtype == ANE_CUDA_F16) {
-            gather_elem_kernel<F16, F16><<<blocks, kGatherWarps * kWarp, 0, s>>>(
+            launch_pdl(gather_elem_kernel<F16, F16>, blocks, kGatherWarps * kWarp, 0, s,
                 (__half*)out, (const __half*)table, ids, rows, vocab, hidden);
         } else {
-            gather_elem_kernel<BF16, BF16><<<blocks, kGatherWarps * kWarp, 0, s>>>(
+            launch_pdl(gather_elem_kernel<BF16, BF16>, blocks, kGatherWarps * kWarp, 0, s,
                 (__nv_bfloat16*)out, (const __nv_bfloat16*)table, ids, rows, vocab, hidden);
         }
     } else if (out_dtype == ANE_CUDA_F32 && table_dtype == ANE_CUDA_F16) {
-        gather_elem_kernel<F16, F32><<<blocks, kGatherWarps * kWarp, 0, s>>>(
+        launch_pdl(gather_elem_kernel<F16, F32>, blocks, kGatherWarps * kWarp, 0, s,
             (float*)out, (const __half*)table, ids, rows, vocab, hidden);
     } else if (out_dtype == ANE_CUDA_F32 && table_dtype == ANE_CUDA_BF16) {
-        gather_elem_kernel<BF16, F32><<<blocks, kGatherWarps * kWarp, 0, s>>>(
+        launch_pdl(gather_elem_kernel<BF16, F32>, blocks, kGatherWarps * kWarp, 0, s,
             (float*)out, (const __nv_bfloat16*)table, ids, rows, vocab, hidden);
     } else {
         return fail(ANE_CUDA_ERR_UNSUPPORTED,

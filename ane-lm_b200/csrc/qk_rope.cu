@@ -72,6 +72,7 @@ constexpr int kRowWarps = 4;
 template <typename T, int GL, int D, bool KV>
 __global__ void __launch_bounds__(kRowWarps * kWarp, KV ? 4 : 8)
 qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim) {
+    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     constexpr int HPW = kWarp / GL;                  // heads per iteration
@@ -237,6 +238,7 @@ constexpr int kGenericMaxHead = 1024;
 template <typename T>
 __global__ void __launch_bounds__(kQkWarps * kWarp)
 qk_norm_rope_generic_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr) {
+    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     __shared__ float sm[kQkWarps][kGenericMaxHead];
@@ -327,8 +329,8 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s, bool k
         const bool pow2 = (a.head_dim & (a.head_dim - 1)) == 0;
 #define ANE_QK_ROW(GLV)                                                                          \
     do {                                                                                          \
-        if (kv) qk_norm_rope_row_kernel<T, GLV, 2, true><<<blocks, kRowWarps * kWarp, 0, s>>>(a, fr, pow2); \
-        else qk_norm_rope_row_kernel<T, GLV, 1, false><<<blocks, kRowWarps * kWarp, 0, s>>>(a, fr, pow2);   \
+        if (kv) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, true>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2); \
+        else launch_pdl(qk_norm_rope_row_kernel<T, GLV, 1, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2);   \
     } while (0)
         switch (gl_log2) {
             case 0: ANE_QK_ROW(1); break;
@@ -344,7 +346,7 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s, bool k
                         kGenericMaxHead);
         const int64_t items = a.rows * nh;
         const unsigned blocks = (unsigned)((items + kQkWarps - 1) / kQkWarps);
-        qk_norm_rope_generic_kernel<T><<<blocks, kQkWarps * kWarp, 0, s>>>(a, fr);
+        launch_pdl(qk_norm_rope_generic_kernel<T>, blocks, kQkWarps * kWarp, 0, s, a, fr);
     }
     return check_launch("qk_norm_rope");
 }

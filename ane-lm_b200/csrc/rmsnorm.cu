@@ -23,6 +23,7 @@ rmsnorm_reg_kernel(typename T::storage* x, int64_t xs,
                    const typename T::storage* __restrict__ d, int64_t ds,
                    typename T::storage* out, int64_t os, const float* __restrict__ w,
                    int64_t rows, int dim, float eps) {
+    pdl_begin();
     constexpr int V = T::kVec;
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
@@ -89,6 +90,7 @@ rmsnorm_2pass_kernel(typename T::storage* x, int64_t xs,
                      const typename T::storage* __restrict__ d, int64_t ds,
                      typename T::storage* out, int64_t os, const float* __restrict__ w,
                      int64_t rows, int dim, float eps) {
+    pdl_begin();
     constexpr int V = T::kVec;
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
@@ -159,16 +161,16 @@ static void launch_rmsnorm(void* x, int64_t xs, const void* d, int64_t ds, void*
     S* op = (S*)out;
     const int per_lane = (dim / V + kWarp - 1) / kWarp;
 #define ANE_NORM_REG(VPL) \
-    rmsnorm_reg_kernel<T, VPL, HAS_D><<<blocks, kNormWarps * kWarp, 0, s>>>(xp, xs, dp, ds, op, os, w, rows, dim, eps)
+    launch_pdl(rmsnorm_reg_kernel<T, VPL, HAS_D>, blocks, kNormWarps * kWarp, 0, s, xp, xs, dp, ds, op, os, w, rows, dim, eps)
     if (vec && per_lane <= 1) ANE_NORM_REG(1);
     else if (vec && per_lane <= 2) ANE_NORM_REG(2);
     else if (vec && per_lane <= 4) ANE_NORM_REG(4);
     else if (vec && per_lane <= 8) ANE_NORM_REG(8);
     else if (vec && per_lane <= 16) ANE_NORM_REG(16);
     else if (vec)
-        rmsnorm_2pass_kernel<T, true, HAS_D><<<blocks, kNormWarps * kWarp, 0, s>>>(xp, xs, dp, ds, op, os, w, rows, dim, eps);
+        launch_pdl(rmsnorm_2pass_kernel<T, true, HAS_D>, blocks, kNormWarps * kWarp, 0, s, xp, xs, dp, ds, op, os, w, rows, dim, eps);
     else
-        rmsnorm_2pass_kernel<T, false, HAS_D><<<blocks, kNormWarps * kWarp, 0, s>>>(xp, xs, dp, ds, op, os, w, rows, dim, eps);
+        launch_pdl(rmsnorm_2pass_kernel<T, false, HAS_D>, blocks, kNormWarps * kWarp, 0, s, xp, xs, dp, ds, op, os, w, rows, dim, eps);
 #undef ANE_NORM_REG
 }
 

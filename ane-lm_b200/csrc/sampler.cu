@@ -253,6 +253,7 @@ __device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, doubl
 
 __global__ void __launch_bounds__(kSampThreads, 2)
 sample_rows_kernel(const SampArgs a) {
+    pdl_begin();
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ RowSmem S;
     __shared__ float cbuf[kSampWarps][kWarp * kPerThread];       // compacted d, then p
@@ -633,6 +634,7 @@ sample_rows_kernel(const SampArgs a) {
 // softmax over rows in place (core/cpu_ops.cpp:83-99) with the pinned sum.
 __global__ void __launch_bounds__(kSampThreads, 2)
 softmax_rows_kernel(float* x, int n, int64_t stride) {
+    pdl_begin();
     __shared__ RowSmem S;
     float* row = x + (int64_t)blockIdx.x * stride;
     const int tid = threadIdx.x;
@@ -706,7 +708,7 @@ int ane_cuda_sample_rows(const float* logits, int64_t rows, int vocab, int64_t l
     SampArgs a{logits, rows, vocab, logits_stride, history, history_len, history_stride, uniforms,
                temperature, repetition_penalty, frequency_penalty, repetition_context, out_tokens,
                slots_log2, vocab % 4 == 0 && logits_stride % 4 == 0 && is_aligned(logits, 16)};
-    sample_rows_kernel<<<(unsigned)rows, kSampThreads, smem, as_stream(stream)>>>(a);
+    launch_pdl(sample_rows_kernel, (unsigned)rows, kSampThreads, smem, as_stream(stream), a);
     return check_launch("sample_rows");
 }
 
@@ -718,7 +720,7 @@ int ane_cuda_softmax_rows(float* x, int64_t rows, int n, int64_t stride, void* s
     if (rows == 0) return ANE_CUDA_OK;
     if (!x) return fail(ANE_CUDA_ERR_INVALID_ARG, "softmax_rows: null pointer");
     if (rows > 0x7fffffffLL) return fail(ANE_CUDA_ERR_UNSUPPORTED, "softmax_rows: too many rows");
-    softmax_rows_kernel<<<(unsigned)rows, kSampThreads, 0, as_stream(stream)>>>(x, n, stride);
+    launch_pdl(softmax_rows_kernel, (unsigned)rows, kSampThreads, 0, as_stream(stream), x, n, stride);
     return check_launch("softmax_rows");
 }
 

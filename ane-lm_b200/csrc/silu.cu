@@ -80,6 +80,7 @@ struct ActArgs {
 template <typename T, int MODE, bool FLAT>
 __global__ void __launch_bounds__(kActThreads)
 act_vec_kernel(const ActArgs p) {
+    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     const int64_t nvec = p.n / V;
@@ -136,6 +137,7 @@ constexpr size_t act_bulk_smem() { return (size_t)kBulkStages * NIN * kBulkTile;
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kActThreads)
 act_bulk_kernel(const ActArgs p, int64_t ntiles, unsigned int* flags) {
+    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     constexpr int NIN = MODE == SILU ? 1 : 2;
@@ -201,6 +203,7 @@ act_bulk_kernel(const ActArgs p, int64_t ntiles, unsigned int* flags) {
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kActThreads)
 act_scalar_kernel(const ActArgs p) {
+    pdl_begin();
     using S = typename T::storage;
     const int64_t total = p.rows * p.n;
     const int64_t stride = (int64_t)gridDim.x * kActThreads;
@@ -237,7 +240,7 @@ static int launch_act(ActArgs p, cudaStream_t s) {
                                                        (int)act_bulk_smem<nin>());
             if (e != cudaSuccess) return fail(ANE_CUDA_ERR_CUDA, "activation: %s", cudaGetErrorString(e));
             const int blocks = resident_grid(kb, kActThreads, act_bulk_smem<nin>(), ntiles);
-            act_bulk_kernel<T, MODE><<<blocks, kActThreads, act_bulk_smem<nin>(), s>>>(p, ntiles, status_flags_device());
+            launch_pdl(act_bulk_kernel<T, MODE>, blocks, kActThreads, act_bulk_smem<nin>(), s, p, ntiles, status_flags_device());
             const int64_t done = ntiles * (kBulkTile / es);
             if (done == p.n) return check_launch("activation");
             const int st = check_launch("activation");
@@ -257,9 +260,9 @@ static int launch_act(ActArgs p, cudaStream_t s) {
                                        : (const void*)act_vec_kernel<T, MODE, false>)
                         : (const void*)act_scalar_kernel<T, MODE>;
     const int blocks = resident_grid(k, kActThreads, 0, want);
-    if (vec && p.rows == 1) act_vec_kernel<T, MODE, true><<<blocks, kActThreads, 0, s>>>(p);
-    else if (vec) act_vec_kernel<T, MODE, false><<<blocks, kActThreads, 0, s>>>(p);
-    else act_scalar_kernel<T, MODE><<<blocks, kActThreads, 0, s>>>(p);
+    if (vec && p.rows == 1) launch_pdl(act_vec_kernel<T, MODE, true>, blocks, kActThreads, 0, s, p);
+    else if (vec) launch_pdl(act_vec_kernel<T, MODE, false>, blocks, kActThreads, 0, s, p);
+    else launch_pdl(act_scalar_kernel<T, MODE>, blocks, kActThreads, 0, s, p);
     return check_launch("activation");
 }
 
