@@ -72,7 +72,7 @@ __device__ __forceinline__ uint4 ld_keep(const void* p) {
 // ---------------------------------------------------------------------
 // programmatic dependent launch
 // ---------------------------------------------------------------------
-// The decode-step kernels are launched with programmatic stream
+// Every kernel of the library is launched with programmatic stream
 // serialisation (launch_pdl): the next kernel on the stream may be
 // dispatched while this one drains, which hides most of the launch gap
 // between the short kernels of a decode step.  A kernel so launched calls

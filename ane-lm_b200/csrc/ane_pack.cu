@@ -107,6 +107,7 @@ template <bool TRUNC, bool VEC>
 __global__ void __launch_bounds__(kPackThreads)
 ane_pack_kernel(uint16_t* __restrict__ surface, const float* __restrict__ in, int64_t in_stride,
                 int64_t tokens, int channels) {
+    pdl_begin();
     __shared__ __align__(16) float tile[kSpatial * kPackCh];
     const int64_t s = blockIdx.x;
     const int c0 = blockIdx.y * kPackCh;
@@ -159,6 +160,7 @@ template <bool VEC>
 __global__ void __launch_bounds__(kPackThreads)
 ane_unpack_kernel(float* __restrict__ out, int64_t out_stride, const uint16_t* __restrict__ surface,
                   int64_t tokens, int channels) {
+    pdl_begin();
     __shared__ __align__(16) float tile[kSpatial * kPackCh];
     const int64_t s = blockIdx.x;
     const int c0 = blockIdx.y * kPackCh;
@@ -206,6 +208,7 @@ ane_unpack_kernel(float* __restrict__ out, int64_t out_stride, const uint16_t* _
 template <bool TRUNC>
 __global__ void ane_pack_any_kernel(uint16_t* surface, const float* in, int64_t in_stride,
                                     int64_t tokens, int channels, int spatial) {
+    pdl_begin();
     const int64_t total = tokens * channels;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -218,6 +221,7 @@ __global__ void ane_pack_any_kernel(uint16_t* surface, const float* in, int64_t 
 
 __global__ void ane_unpack_any_kernel(float* out, int64_t out_stride, const uint16_t* surface,
                                       int64_t tokens, int channels, int spatial) {
+    pdl_begin();
     const int64_t total = tokens * channels;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -257,17 +261,17 @@ int ane_cuda_ane_pack(int round_mode, uint16_t* surface, const float* in, int64_
         if (grid.y > 65535) return fail(ANE_CUDA_ERR_UNSUPPORTED, "ane_pack: %d channels", channels);
         const bool vec = is_aligned(in, 16) && in_stride % 4 == 0;
         if (trunc) {
-            if (vec) ane_pack_kernel<true, true><<<grid, kPackThreads, 0, s>>>(surface, in, in_stride, tokens, channels);
-            else ane_pack_kernel<true, false><<<grid, kPackThreads, 0, s>>>(surface, in, in_stride, tokens, channels);
+            if (vec) launch_pdl(ane_pack_kernel<true, true>, grid, kPackThreads, 0, s, surface, in, in_stride, tokens, channels);
+            else launch_pdl(ane_pack_kernel<true, false>, grid, kPackThreads, 0, s, surface, in, in_stride, tokens, channels);
         } else {
-            if (vec) ane_pack_kernel<false, true><<<grid, kPackThreads, 0, s>>>(surface, in, in_stride, tokens, channels);
-            else ane_pack_kernel<false, false><<<grid, kPackThreads, 0, s>>>(surface, in, in_stride, tokens, channels);
+            if (vec) launch_pdl(ane_pack_kernel<false, true>, grid, kPackThreads, 0, s, surface, in, in_stride, tokens, channels);
+            else launch_pdl(ane_pack_kernel<false, false>, grid, kPackThreads, 0, s, surface, in, in_stride, tokens, channels);
         }
     } else {
         const int blocks = resident_grid(reinterpret_cast<const void*>(ane_pack_any_kernel<false>), 256, 0,
                                          (tokens * channels + 255) / 256);
-        if (trunc) ane_pack_any_kernel<true><<<blocks, 256, 0, s>>>(surface, in, in_stride, tokens, channels, spatial);
-        else ane_pack_any_kernel<false><<<blocks, 256, 0, s>>>(surface, in, in_stride, tokens, channels, spatial);
+        if (trunc) launch_pdl(ane_pack_any_kernel<true>, blocks, 256, 0, s, surface, in, in_stride, tokens, channels, spatial);
+        else launch_pdl(ane_pack_any_kernel<false>, blocks, 256, 0, s, surface, in, in_stride, tokens, channels, spatial);
     }
     return check_launch("ane_pack");
 }
@@ -283,13 +287,13 @@ int ane_cuda_ane_unpack(float* out, int64_t out_stride, const uint16_t* surface,
                         (unsigned)((channels + kPackCh - 1) / kPackCh));
         if (grid.y > 65535) return fail(ANE_CUDA_ERR_UNSUPPORTED, "ane_unpack: %d channels", channels);
         if (is_aligned(out, 16) && out_stride % 4 == 0)
-            ane_unpack_kernel<true><<<grid, kPackThreads, 0, s>>>(out, out_stride, surface, tokens, channels);
+            launch_pdl(ane_unpack_kernel<true>, grid, kPackThreads, 0, s, out, out_stride, surface, tokens, channels);
         else
-            ane_unpack_kernel<false><<<grid, kPackThreads, 0, s>>>(out, out_stride, surface, tokens, channels);
+            launch_pdl(ane_unpack_kernel<false>, grid, kPackThreads, 0, s, out, out_stride, surface, tokens, channels);
     } else {
         const int blocks = resident_grid(reinterpret_cast<const void*>(ane_unpack_any_kernel), 256, 0,
                                          (tokens * channels + 255) / 256);
-        ane_unpack_any_kernel<<<blocks, 256, 0, s>>>(out, out_stride, surface, tokens, channels, spatial);
+        launch_pdl(ane_unpack_any_kernel, blocks, 256, 0, s, out, out_stride, surface, tokens, channels, spatial);
     }
     return check_launch("ane_unpack");
 }

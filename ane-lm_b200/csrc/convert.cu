@@ -55,6 +55,7 @@ constexpr int kConvUnroll = 4;
 // Vector path: in/out 16-byte aligned, nvec 8-element vectors.
 __global__ void __launch_bounds__(kConvThreads)
 bf16_to_f16_vec_kernel(uint4* __restrict__ out, const uint4* __restrict__ in, int64_t nvec) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * kConvThreads;
     int64_t i = (int64_t)blockIdx.x * kConvThreads + threadIdx.x;
     // Main loop: kConvUnroll independent vectors per thread in flight.
@@ -82,6 +83,7 @@ constexpr size_t kConvSmem = (size_t)kConvStages * kConvTile;
 __global__ void __launch_bounds__(kConvThreads)
 bf16_to_f16_bulk_kernel(uint4* __restrict__ out, const uint4* __restrict__ in, int64_t ntiles,
                         unsigned int* flags) {
+    pdl_begin();
     constexpr int VPT = kConvTile / 16;          // 16-byte vectors per tile
     constexpr int STEPS = VPT / kConvThreads;    // per thread
     extern __shared__ __align__(128) unsigned char smem[];
@@ -134,6 +136,7 @@ bf16_to_f16_bulk_kernel(uint4* __restrict__ out, const uint4* __restrict__ in, i
 // Scalar path for the ragged tail or unaligned buffers.
 __global__ void bf16_to_f16_scalar_kernel(uint16_t* __restrict__ out,
                                           const uint16_t* __restrict__ in, int64_t n) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
         out[i] = (uint16_t)bf16_to_f16_bits(in[i]);
@@ -155,7 +158,7 @@ extern "C" int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t n
                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kConvSmem);
         if (e != cudaSuccess) return fail(ANE_CUDA_ERR_CUDA, "bf16_to_f16: %s", cudaGetErrorString(e));
         const int blocks = resident_grid((const void*)bf16_to_f16_bulk_kernel, kConvThreads, kConvSmem, ntiles);
-        bf16_to_f16_bulk_kernel<<<blocks, kConvThreads, kConvSmem, s>>>(
+        launch_pdl(bf16_to_f16_bulk_kernel, blocks, kConvThreads, kConvSmem, s,
             reinterpret_cast<uint4*>(out), reinterpret_cast<const uint4*>(in), ntiles, status_flags_device());
         done = ntiles * (kConvTile / 2);
     }
@@ -163,14 +166,14 @@ extern "C" int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t n
         const int64_t nvec = (n - done) / 8;
         const int64_t want = (nvec + kConvThreads * kConvUnroll - 1) / (kConvThreads * kConvUnroll);
         const int blocks = resident_grid((const void*)bf16_to_f16_vec_kernel, kConvThreads, 0, want);
-        bf16_to_f16_vec_kernel<<<blocks, kConvThreads, 0, s>>>(
+        launch_pdl(bf16_to_f16_vec_kernel, blocks, kConvThreads, 0, s,
             reinterpret_cast<uint4*>(out + done), reinterpret_cast<const uint4*>(in + done), nvec);
         done += nvec * 8;
     }
     if (done < n) {
         const int64_t rest = n - done;
         const int blocks = (int)((rest + 255) / 256 < (int64_t)sms * 4 ? (rest + 255) / 256 : (int64_t)sms * 4);
-        bf16_to_f16_scalar_kernel<<<blocks, 256, 0, s>>>(out + done, in + done, rest);
+        launch_pdl(bf16_to_f16_scalar_kernel, blocks, 256, 0, s, out + done, in + done, rest);
     }
     return check_launch("bf16_to_f16");
 }

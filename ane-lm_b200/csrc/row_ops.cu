@@ -55,6 +55,7 @@ __device__ __forceinline__ float row_out(float x, float inv, float z, float w, f
 template <typename T, int MODE, int VPL>
 __global__ void __launch_bounds__(kRowWarps * kWarp)
 row_reg_kernel(const RowArgs a) {
+    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     const int lane = threadIdx.x & 31;
@@ -104,6 +105,7 @@ row_reg_kernel(const RowArgs a) {
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kRowWarps * kWarp)
 row_any_kernel(const RowArgs a) {
+    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     const int lane = threadIdx.x & 31;
@@ -148,12 +150,12 @@ static int launch_row(const RowArgs& a, cudaStream_t s) {
         vec = vec && is_aligned(a.z, 16) && is_aligned(a.w, 16) && (a.zs * es) % 16 == 0;
     const int per_lane = (a.dim / V + kWarp - 1) / kWarp;
     const int threads = kRowWarps * kWarp;
-    if (vec && per_lane <= 1) row_reg_kernel<T, MODE, 1><<<blocks, threads, 0, s>>>(a);
-    else if (vec && per_lane <= 2) row_reg_kernel<T, MODE, 2><<<blocks, threads, 0, s>>>(a);
-    else if (vec && per_lane <= 4) row_reg_kernel<T, MODE, 4><<<blocks, threads, 0, s>>>(a);
-    else if (vec && per_lane <= 8) row_reg_kernel<T, MODE, 8><<<blocks, threads, 0, s>>>(a);
-    else if (vec && per_lane <= 16) row_reg_kernel<T, MODE, 16><<<blocks, threads, 0, s>>>(a);
-    else row_any_kernel<T, MODE><<<blocks, threads, 0, s>>>(a);
+    if (vec && per_lane <= 1) launch_pdl(row_reg_kernel<T, MODE, 1>, blocks, threads, 0, s, a);
+    else if (vec && per_lane <= 2) launch_pdl(row_reg_kernel<T, MODE, 2>, blocks, threads, 0, s, a);
+    else if (vec && per_lane <= 4) launch_pdl(row_reg_kernel<T, MODE, 4>, blocks, threads, 0, s, a);
+    else if (vec && per_lane <= 8) launch_pdl(row_reg_kernel<T, MODE, 8>, blocks, threads, 0, s, a);
+    else if (vec && per_lane <= 16) launch_pdl(row_reg_kernel<T, MODE, 16>, blocks, threads, 0, s, a);
+    else launch_pdl(row_any_kernel<T, MODE>, blocks, threads, 0, s, a);
     return check_launch(MODE == kGated ? "rmsnorm_gated" : "l2_normalize");
 }
 
@@ -167,6 +169,7 @@ static int run_row(int dtype, const RowArgs& a, cudaStream_t s) {
 // bf16 bits -> f32, optionally + 1.0f; 8 elements per thread step.
 __global__ void bf16_to_f32_kernel(float* __restrict__ out, const uint16_t* __restrict__ in,
                                    int64_t n, int add_one, int vec) {
+    pdl_begin();
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     const int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     // NaN + 1 keeps the (quieted) NaN operand on the CPU; the GPU adder
@@ -234,7 +237,7 @@ int ane_cuda_bf16_to_f32(float* out, const uint16_t* in, int64_t n, int add_one,
     const int vec = is_aligned(out, 16) && is_aligned(in, 16);
     const int blocks = resident_grid(reinterpret_cast<const void*>(bf16_to_f32_kernel), 256, 0,
                                      (n / 8 + 255) / 256 + 1);
-    bf16_to_f32_kernel<<<blocks, 256, 0, as_stream(stream)>>>(out, in, n, add_one != 0, vec);
+    launch_pdl(bf16_to_f32_kernel, blocks, 256, 0, as_stream(stream), out, in, n, add_one != 0, vec);
     return check_launch("bf16_to_f32");
 }
 
