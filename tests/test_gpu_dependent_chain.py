@@ -1,0 +1,104 @@
+"""Back-to-back dependent launches.
+
+Every kernel of the library is launched with programmatic stream
+serialisation, so the next kernel on a stream may be dispatched while the
+previous one is still running; each kernel waits (griddepcontrol.wait)
+before its first global-memory access.  These tests run a decode-step
+chain in which each kernel reads what the one before it wrote -- gather ->
+residual + RMSNorm (reads the gathered rows) -> QK-norm + RoPE in place on
+the normalised rows -> SiLU-gate of halves of those rows -- with no host
+synchronisation in between, eagerly and replayed from a captured CUDA
+graph, and check every intermediate bit for bit against the oracle chain
+(fp32).  A torch copy kernel at the head of the graph also checks the wait
+through a kernel launched without the attribute."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROWS, HIDDEN, VOCAB = 8, 1024, 5000
+NQ, NKV, HD = 4, 2, 128  # (4 + 2 + 2) x 128 = HIDDEN: the q/k/v layout over the normed rows
+
+
+def _inputs(torch, seed):
+    rng = np.random.default_rng(seed)
+    table = (rng.standard_normal((VOCAB, HIDDEN)) * 0.5).astype(np.float16)
+    ids = rng.integers(0, VOCAB, ROWS).astype(np.int32)
+    x = rng.standard_normal((ROWS, HIDDEN)).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32)
+    pos = rng.integers(0, 4096, ROWS).astype(np.int32)
+    return table, ids, x, w, pos
+
+
+def _oracle_chain(oracle, table, ids, x, w, pos):
+    xe, bad = oracle.embedding_gather(table, ids, out_dtype=0)
+    assert bad == 0
+    x_after, y = oracle.residual_rmsnorm(x, xe, w)
+    y = oracle.qk_norm_rope(y, NQ, NKV, HD, w[:HD], w[HD:2 * HD], pos, 1e6)
+    h = oracle.silu_mul(np.ascontiguousarray(y[:, :HIDDEN // 2]),
+                        np.ascontiguousarray(y[:, HIDDEN // 2:]))
+    return xe, x_after, y, h
+
+
+class _Chain:
+    def __init__(self, torch, ane, table, ids, x, w, pos):
+        self.torch, self.ane = torch, ane
+        self.table = torch.from_numpy(table).cuda()
+        self.ids = torch.from_numpy(ids).cuda()
+        self.x0 = torch.from_numpy(x).cuda()
+        self.x = self.x0.clone()
+        self.w = torch.from_numpy(w).cuda()
+        self.qw = self.w[:HD].clone()
+        self.kw = self.w[HD:2 * HD].clone()
+        self.pos = torch.from_numpy(pos).cuda()
+        self.xe = torch.empty(ROWS, HIDDEN, device="cuda")
+        self.y = torch.empty(ROWS, HIDDEN, device="cuda")
+        self.h = torch.empty(ROWS, HIDDEN // 2, device="cuda")
+
+    def run(self):
+        ane, half = self.ane, HIDDEN // 2
+        self.x.copy_(self.x0)  # a torch kernel, launched without the attribute
+        ane.embedding_gather(self.table, self.ids, out_dtype=self.torch.float32, out=self.xe)
+        ane.residual_rmsnorm(self.x, self.xe, self.w, out=self.y)
+        ane.qk_norm_rope(self.y, self.qw, self.kw, self.pos, NQ, NKV, HD)
+        ane.silu_mul(self.y[:, :half], self.y[:, half:], out=self.h)
+
+    def results(self):
+        return [t.cpu().numpy() for t in (self.xe, self.x, self.y, self.h)]
+
+
+def _same(got, want):
+    for name, g, e in zip(("gather", "residual", "qk", "silu"), got, want):
+        assert np.array_equal(g.view(np.uint32), e.view(np.uint32)), name
+
+
+def test_dependent_chain_eager(ane, oracle):
+    import torch
+    table, ids, x, w, pos = _inputs(torch, 41)
+    want = _oracle_chain(oracle, table, ids, x, w, pos)
+    ch = _Chain(torch, ane, table, ids, x, w, pos)
+    for _ in range(3):  # repeated without synchronising in between
+        ch.run()
+    torch.cuda.synchronize()
+    _same(ch.results(), want)
+
+
+def test_dependent_chain_graph_replay(ane, oracle):
+    import torch
+    table, ids, x, w, pos = _inputs(torch, 42)
+    want = _oracle_chain(oracle, table, ids, x, w, pos)
+    ch = _Chain(torch, ane, table, ids, x, w, pos)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ch.run()  # warm-up outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        ch.run()
+    for _ in range(5):
+        ch.y.zero_()
+        ch.h.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    _same(ch.results(), want)
+    del g
