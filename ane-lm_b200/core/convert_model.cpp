@@ -1,18 +1,32 @@
 // convert_model.cpp -- `ane-lm convert` with the conversion on the GPU.
 //
 // For each shard (core/model_loader.cpp:163-171) and each BF16 tensor of it
-// in header order (core/safetensors.cpp:345-383): create the parent
-// directories, write the 128-byte blob header, and stream the tensor through
-// two pinned staging slots: copy from the mapping into pinned memory, H2D,
-// ane_cuda_bf16_to_f16, D2H, write.  While the GPU works on one slot the host
-// fills or drains the other.  Non-BF16 tensors are skipped, as the reference
-// does.  The output tree is byte-identical to the reference writer's.
+// (core/safetensors.cpp:345-383): create the parent directories, write the
+// 128-byte blob header, and stream the tensor through two pinned staging
+// slots: read from the shard into pinned memory (pread: no page faults on a
+// shared mapping), H2D, ane_cuda_bf16_to_f16, D2H, write.  While the GPU works on one slot the
+// host fills or drains the other.  Every tensor is its own output file, so
+// the tensors are shared out among a few worker threads, each with its own
+// stream and staging slots: the host copies and file writes, which bound
+// the conversion, run in parallel.  Non-BF16 tensors are skipped, as the
+// reference does.  The output tree is byte-identical to the reference
+// writer's.
 #include <cuda_runtime.h>
 
+#include <fcntl.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cerrno>
 #include <cstdio>
 #include <cstring>
 #include <filesystem>
+#include <memory>
+#include <mutex>
 #include <string>
+#include <thread>
+#include <vector>
 
 #include "ane_cuda.h"
 #include "ane_internal.h"
@@ -56,9 +70,24 @@ struct Stage {
     }
 };
 
-// Writes one BF16 tensor as an ANE blob.
-int write_blob(Stage& st, cudaStream_t s, const std::string& path, const uint16_t* src,
-               int64_t n) {
+// Reads `bytes` at `offset` of fd into dst; false on a short read or error.
+bool read_at(int fd, void* dst, size_t bytes, uint64_t offset) {
+    uint8_t* p = static_cast<uint8_t*>(dst);
+    while (bytes > 0) {
+        const ssize_t r = pread(fd, p, bytes, (off_t)offset);
+        if (r < 0 && errno == EINTR) continue;
+        if (r <= 0) return false;
+        p += r;
+        bytes -= (size_t)r;
+        offset += (uint64_t)r;
+    }
+    return true;
+}
+
+// Writes one BF16 tensor (n elements at byte `src_offset` of shard fd) as an
+// ANE blob.
+int write_blob(Stage& st, cudaStream_t s, const std::string& path, int src_fd,
+               uint64_t src_offset, int64_t n) {
     std::error_code ec;
     std::filesystem::create_directories(std::filesystem::path(path).parent_path(), ec);
     FILE* f = fopen(path.c_str(), "wb");
@@ -82,7 +111,10 @@ int write_blob(Stage& st, cudaStream_t s, const std::string& path, const uint16_
         const int slot = (int)(chunk & 1);
         drain(slot);  // the chunk two back, written in order
         const size_t m = (size_t)((n - off) < (int64_t)kChunkElems ? (n - off) : (int64_t)kChunkElems);
-        memcpy(st.h_in[slot], src + off, m * 2);
+        if (!read_at(src_fd, st.h_in[slot], m * 2, src_offset + (uint64_t)off * 2)) {
+            status = set_err(ANE_CUDA_ERR_INVALID_ARG, "convert: short read of a tensor for " + path);
+            break;
+        }
         cudaError_t e = cudaMemcpyAsync(st.d_in[slot], st.h_in[slot], m * 2, cudaMemcpyHostToDevice, s);
         if (e != cudaSuccess) { status = set_err(ANE_CUDA_ERR_CUDA, cudaGetErrorString(e)); break; }
         const int kst = ane_cuda_bf16_to_f16(st.d_out[slot], st.d_in[slot], (int64_t)m, s);
@@ -101,21 +133,86 @@ int write_blob(Stage& st, cudaStream_t s, const std::string& path, const uint16_
     return status;
 }
 
-int write_file_blobs(Stage& st, cudaStream_t s, const std::string& path,
-                     const std::string& out_dir, int64_t* written) {
-    SafetensorsFile sf;
-    std::string err;
-    if (!sf.open(path, &err)) return set_err(ANE_CUDA_ERR_INVALID_ARG, err);
+// One blob to write: a BF16 tensor of a mapped shard.
+struct Job {
+    const std::string* file;  // the shard
+    uint64_t offset;          // of the tensor's data in the shard
+    int64_t n;
+    std::string path;
+};
+
+// Adds the BF16 tensors of one opened shard to `jobs`, in header order.
+int collect_jobs(const SafetensorsFile& sf, const std::string& out_dir, std::vector<Job>* jobs) {
     for (const TensorInfo& t : sf.tensors()) {
         if (t.dtype != TensorDtype::BF16) continue;
         const int64_t n = t.numel();
         if ((uint64_t)n * 2 > t.end - t.begin)
             return set_err(ANE_CUDA_ERR_INVALID_ARG, "tensor '" + t.name + "' is shorter than its shape");
-        const int rc = write_blob(st, s, ane_blob_path(out_dir, t.name),
-                                  reinterpret_cast<const uint16_t*>(sf.data(t)), n);
-        if (rc != ANE_CUDA_OK) return rc;
-        (*written)++;
+        jobs->push_back({&sf.path(), sf.file_offset(t), n, ane_blob_path(out_dir, t.name)});
     }
+    return ANE_CUDA_OK;
+}
+
+constexpr int kMaxWorkers = 4;
+
+// Writes every job, on up to kMaxWorkers threads of the calling thread's
+// device, each with its own stream and staging slots.  Work queued on
+// `stream` before the call completes first.  The first failure stops the
+// workers and is reported (with its message) on the calling thread.
+int run_jobs(const std::vector<Job>& jobs, cudaStream_t stream, int64_t* written) {
+    if (jobs.empty()) return ANE_CUDA_OK;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return set_err(ANE_CUDA_ERR_CUDA, std::string("convert: ") + cudaGetErrorString(e));
+    const unsigned hw = std::thread::hardware_concurrency();
+    const int nw = (int)std::min<size_t>(jobs.size(), std::max(1u, std::min<unsigned>(kMaxWorkers, hw ? hw : 1)));
+    std::atomic<size_t> next{0};
+    std::atomic<int64_t> done{0};
+    std::atomic<bool> failed{false};
+    std::mutex mu;
+    int first_status = ANE_CUDA_OK;
+    std::string first_msg;
+    auto record = [&](int st, const std::string& msg) {
+        std::lock_guard<std::mutex> lock(mu);
+        if (first_status == ANE_CUDA_OK) {
+            first_status = st;
+            first_msg = msg;
+        }
+        failed = true;
+    };
+    auto worker = [&]() {
+        cudaError_t we = cudaSetDevice(dev);
+        cudaStream_t ws = nullptr;
+        if (we == cudaSuccess) we = cudaStreamCreateWithFlags(&ws, cudaStreamNonBlocking);
+        Stage st;
+        if (we == cudaSuccess) we = st.init();
+        if (we != cudaSuccess) {
+            record(ANE_CUDA_ERR_CUDA, std::string("convert: ") + cudaGetErrorString(we));
+        } else {
+            for (size_t i = next++; i < jobs.size() && !failed; i = next++) {
+                const int fd = ::open(jobs[i].file->c_str(), O_RDONLY);
+                if (fd < 0) {
+                    record(ANE_CUDA_ERR_INVALID_ARG, "convert: cannot read " + *jobs[i].file);
+                    break;
+                }
+                const int rc = write_blob(st, ws, jobs[i].path, fd, jobs[i].offset, jobs[i].n);
+                ::close(fd);
+                if (rc != ANE_CUDA_OK) {
+                    record(rc, ane_cuda_last_error());  // the message is this thread's
+                    break;
+                }
+                done++;
+            }
+        }
+        if (ws) cudaStreamDestroy(ws);
+    };
+    std::vector<std::thread> pool;
+    for (int w = 1; w < nw; w++) pool.emplace_back(worker);
+    worker();  // the calling thread is worker 0
+    for (std::thread& t : pool) t.join();
+    *written += done;
+    if (first_status != ANE_CUDA_OK) return set_err(first_status, first_msg);
     return ANE_CUDA_OK;
 }
 
@@ -131,11 +228,13 @@ int ane_cuda_write_ane_blobs(const char* safetensors_path, const char* output_di
     if (!safetensors_path || !output_dir || !written)
         return set_err(ANE_CUDA_ERR_INVALID_ARG, "write_ane_blobs: null argument");
     *written = 0;
-    Stage st;
-    const cudaError_t e = st.init();
-    if (e != cudaSuccess)
-        return set_err(ANE_CUDA_ERR_CUDA, std::string("write_ane_blobs: ") + cudaGetErrorString(e));
-    return write_file_blobs(st, static_cast<cudaStream_t>(stream), safetensors_path, output_dir, written);
+    SafetensorsFile sf;
+    std::string err;
+    if (!sf.open(safetensors_path, &err)) return set_err(ANE_CUDA_ERR_INVALID_ARG, err);
+    std::vector<Job> jobs;
+    const int rc = collect_jobs(sf, output_dir, &jobs);
+    if (rc != ANE_CUDA_OK) return rc;
+    return run_jobs(jobs, static_cast<cudaStream_t>(stream), written);
 }
 
 int ane_cuda_convert_model(const char* model_dir, const char* output_dir, int64_t* written,
@@ -147,15 +246,16 @@ int ane_cuda_convert_model(const char* model_dir, const char* output_dir, int64_
     std::vector<std::string> shards;
     std::string err;
     if (!discover_shards(model_dir, &shards, &err)) return set_err(ANE_CUDA_ERR_INVALID_ARG, err);
-    Stage st;
-    const cudaError_t e = st.init();
-    if (e != cudaSuccess)
-        return set_err(ANE_CUDA_ERR_CUDA, std::string("convert_model: ") + cudaGetErrorString(e));
+    // every shard mapped for the whole conversion (address space only)
+    std::vector<std::unique_ptr<SafetensorsFile>> files;
+    std::vector<Job> jobs;
     for (const std::string& shard : shards) {
-        const int rc = write_file_blobs(st, static_cast<cudaStream_t>(stream), shard, output_dir, written);
+        files.push_back(std::make_unique<SafetensorsFile>());
+        if (!files.back()->open(shard, &err)) return set_err(ANE_CUDA_ERR_INVALID_ARG, err);
+        const int rc = collect_jobs(*files.back(), output_dir, &jobs);
         if (rc != ANE_CUDA_OK) return rc;
     }
-    return ANE_CUDA_OK;
+    return run_jobs(jobs, static_cast<cudaStream_t>(stream), written);
 }
 
 }  // extern "C"

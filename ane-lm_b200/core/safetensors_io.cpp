@@ -199,6 +199,7 @@ SafetensorsFile::~SafetensorsFile() {
 }
 
 bool SafetensorsFile::open(const std::string& path, std::string* err) {
+    path_ = path;
     const int fd = ::open(path.c_str(), O_RDONLY);
     if (fd < 0) { *err = "cannot open " + path; return false; }
     struct stat st;

@@ -34,8 +34,14 @@ public:
     const std::vector<TensorInfo>& tensors() const { return tensors_; }
     const uint8_t* data(const TensorInfo& t) const { return data_ + t.begin; }
     size_t data_bytes() const { return data_bytes_; }
+    // byte offset of a tensor's data in the file, and the file's path
+    uint64_t file_offset(const TensorInfo& t) const {
+        return (uint64_t)(data_ - static_cast<const uint8_t*>(map_)) + t.begin;
+    }
+    const std::string& path() const { return path_; }
 
 private:
+    std::string path_;
     void* map_ = nullptr;
     size_t map_size_ = 0;
     const uint8_t* data_ = nullptr;

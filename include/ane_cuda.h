@@ -70,8 +70,10 @@ ANE_CUDA_API int ane_cuda_bf16_to_f16(uint16_t* out, const uint16_t* in, int64_t
 
 /* ---- `ane-lm convert` ----------------------------------------------------
  * HOST paths, not device pointers.  The conversion runs on the calling
- * thread's current device; staging (128 MiB pinned, 128 MiB device) is
- * allocated per call.  Output files are byte-identical to the reference's.
+ * thread's current device, on up to 4 threads (the caller's and 3 more),
+ * each with its own stream and staging (128 MiB pinned, 128 MiB device,
+ * allocated per call); work already queued on `stream` completes first.
+ * Output files are byte-identical to the reference's.
  *
  * ane_cuda_write_ane_blobs replaces SafeTensors::write_ane_blobs
  * (core/safetensors.cpp:345-383, blob format :316-343): every BF16 tensor of
