@@ -26,6 +26,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <unordered_set>
 #include <vector>
 
 #include "ane_cuda.h"
@@ -167,6 +168,16 @@ int run_jobs(const std::vector<Job>& jobs, cudaStream_t stream, int64_t* written
     if (e != cudaSuccess) return set_err(ANE_CUDA_ERR_CUDA, std::string("convert: ") + cudaGetErrorString(e));
     const unsigned hw = std::thread::hardware_concurrency();
     const int nw = (int)std::min<size_t>(jobs.size(), std::max(1u, std::min<unsigned>(kMaxWorkers, hw ? hw : 1)));
+    // A later job for the same output file (a tensor repeated in a later
+    // shard) overwrites it in the reference, which writes in order: only the
+    // last job per path runs, the earlier ones count as written.  So no two
+    // workers ever write one file, and the tree is the reference's.
+    std::vector<char> superseded(jobs.size(), 0);
+    {
+        std::unordered_set<std::string> seen;
+        for (size_t i = jobs.size(); i-- > 0;)
+            if (!seen.insert(jobs[i].path).second) superseded[i] = 1;
+    }
     std::atomic<size_t> next{0};
     std::atomic<int64_t> done{0};
     std::atomic<bool> failed{false};
@@ -191,6 +202,10 @@ int run_jobs(const std::vector<Job>& jobs, cudaStream_t stream, int64_t* written
             record(ANE_CUDA_ERR_CUDA, std::string("convert: ") + cudaGetErrorString(we));
         } else {
             for (size_t i = next++; i < jobs.size() && !failed; i = next++) {
+                if (superseded[i]) {
+                    done++;
+                    continue;
+                }
                 const int fd = ::open(jobs[i].file->c_str(), O_RDONLY);
                 if (fd < 0) {
                     record(ANE_CUDA_ERR_INVALID_ARG, "convert: cannot read " + *jobs[i].file);

@@ -77,3 +77,47 @@ def test_recursive_discovery_without_index(ane, oracle, tmp_path):
     tree = read_tree(out)
     assert tree["x/y.bin"] == blob_bytes(oracle.bf16_to_f16(a.ravel()))
     assert tree["z.bin"] == blob_bytes(oracle.bf16_to_f16(b))
+
+
+def test_repeated_tensors_last_shard_wins(ane, oracle, tmp_path):
+    """Tensors repeated across shards: the reference writes shards in order, so
+    the last shard's data ends in the file, and every write is counted.  The
+    conversion runs on several threads; the result must not depend on them."""
+    rng = np.random.default_rng(3)
+    md = tmp_path / "model"
+    md.mkdir()
+    names = [f"model.layers.{i}.self_attn.q_proj.weight" for i in range(6)]
+    wm, last = {}, {}
+    for sh in range(3):
+        fn = f"model-{sh + 1:05d}-of-00003.safetensors"
+        tensors = []
+        for i, n in enumerate(names):
+            a = rng.integers(0, 65536, size=(64, 1000 + 37 * i + sh), dtype=np.uint16)
+            tensors.append((n, "BF16", a))
+            last[n] = a
+            wm[n] = fn
+        write_safetensors(md / fn, tensors)
+    (md / "model.safetensors.index.json").write_text(
+        json.dumps({"weight_map": {f"t{i}": f"model-{i % 3 + 1:05d}-of-00003.safetensors"
+                                   for i in range(3)}}))
+    out = tmp_path / "out"
+    for _ in range(2):  # the second run overwrites the same tree
+        assert ane.convert_model(str(md), str(out)) == 18
+        tree = read_tree(out)
+        assert set(tree) == {n.replace(".", "/") + ".bin" for n in names}
+        for n in names:
+            assert tree[n.replace(".", "/") + ".bin"] == blob_bytes(oracle.bf16_to_f16(last[n].ravel())), n
+
+
+def test_write_failure_in_a_worker_is_reported(ane, tmp_path):
+    """A blob that cannot be created (its directory is a file) fails the call
+    with the message of the thread that met it."""
+    rng = np.random.default_rng(4)
+    st = tmp_path / "model.safetensors"
+    write_safetensors(st, [(f"w{i}.weight", "BF16", rng.integers(0, 65536, 5000, dtype=np.uint16))
+                           for i in range(8)])
+    out = tmp_path / "out"
+    out.write_text("not a directory")
+    with pytest.raises(ane.AneCudaError) as e:
+        ane.write_ane_blobs(str(st), str(out))
+    assert "cannot write" in str(e.value)
