@@ -10,7 +10,10 @@ the normalised rows -> SiLU-gate of halves of those rows -- with no host
 synchronisation in between, eagerly and replayed from a captured CUDA
 graph, and check every intermediate bit for bit against the oracle chain
 (fp32).  A torch copy kernel at the head of the graph also checks the wait
-through a kernel launched without the attribute."""
+through a kernel launched without the attribute.  A second test runs the
+decode step's KV write (QK-norm + RoPE writing q in place and k / v into
+the ring) followed at once by decode attention over that ring, against the
+same two calls with a device synchronisation between them."""
 import numpy as np
 import pytest
 
@@ -101,4 +104,64 @@ def test_dependent_chain_graph_replay(ane, oracle):
         g.replay()
     torch.cuda.synchronize()
     _same(ch.results(), want)
+    del g
+
+
+def _decode_step_inputs(torch, seed, B=16, nq=32, nkv=8, hd=128, cap=1024):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    qkv = torch.randn(B, (nq + 2 * nkv) * hd, generator=g).half().cuda()
+    kc = torch.randn(B, cap, nkv, hd, generator=g).half().cuda()
+    vc = torch.randn(B, cap, nkv, hd, generator=g).half().cuda()
+    start = torch.randint(0, cap, (B,), generator=g, dtype=torch.int32)
+    ln = torch.randint(1, cap, (B,), generator=g, dtype=torch.int32)
+    slots = ((start + ln) % cap).to(torch.int32)  # the new token's ring slot
+    w = (1 + 0.1 * torch.randn(2, hd, generator=g)).float().cuda()
+    pos = ln.clone()
+    return dict(qkv=qkv, kc=kc, vc=vc, start=start.cuda(), ln=(ln + 1).cuda(), slots=slots.cuda(),
+                qw=w[0].clone(), kw=w[1].clone(), pos=pos.cuda(), nq=nq, nkv=nkv, hd=hd)
+
+
+def _decode_step(torch, ane, t, sync_between):
+    B = t["qkv"].shape[0]
+    ane.qk_norm_rope_kv(t["qkv"], t["qw"], t["kw"], t["pos"], t["nq"], t["nkv"], t["hd"],
+                        t["kc"], t["vc"], t["slots"])
+    if sync_between:
+        torch.cuda.synchronize()
+    q = t["qkv"][:, :t["nq"] * t["hd"]].view(B, t["nq"], t["hd"])
+    return ane.decode_attention(q, t["kc"], t["vc"], t["start"], t["ln"])
+
+
+def test_decode_step_kv_write_then_attention(ane):
+    """The decode step's QK-norm + RoPE writes q in place and the new k / v
+    into the ring; attention, launched right after, reads both (q through
+    the read-only path, the ring through asynchronous copies).  Same bits as
+    with a device synchronisation between the two."""
+    import torch
+    base = _decode_step_inputs(torch, 43)
+    want_t = {k: (v.clone() if hasattr(v, "clone") else v) for k, v in base.items()}
+    want = _decode_step(torch, ane, want_t, sync_between=True)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        t = {k: (v.clone() if hasattr(v, "clone") else v) for k, v in base.items()}
+        got = _decode_step(torch, ane, t, sync_between=False)
+        torch.cuda.synchronize()
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+        assert torch.equal(t["kc"].view(torch.int16), want_t["kc"].view(torch.int16))
+        assert torch.equal(t["vc"].view(torch.int16), want_t["vc"].view(torch.int16))
+
+    # the same step replayed from a captured graph, inputs restored inside it
+    t = {k: (v.clone() if hasattr(v, "clone") else v) for k, v in base.items()}
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        _decode_step(torch, ane, t, sync_between=False)  # warm-up (workspace, instances)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for key in ("qkv", "kc", "vc"):
+            t[key].copy_(base[key])
+        out = _decode_step(torch, ane, t, sync_between=False)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), want.view(torch.int16))
     del g
