@@ -78,6 +78,34 @@ int held_workspace(cudaStream_t s, int64_t need, void** out) {
     return ANE_CUDA_OK;
 }
 
+// The split counters must read zero when a call starts; every call leaves
+// its own counters at zero.  A call with another layout (batch, heads,
+// head_dim, splits) puts its counters over bytes where the previous call on
+// that workspace kept split partials, so the layout last used with each
+// workspace is remembered and, when it changes, the new counters are
+// cleared on the stream ahead of the kernel.
+std::mutex g_layout_mu;
+std::unordered_map<const void*, uint64_t>* g_layout = nullptr;
+
+int clear_counters_on_layout_change(const AttnArgs& a, const void* ws, int64_t batch,
+                                    int head_dim, cudaStream_t s) {
+    const uint64_t sig = ((uint64_t)batch << 40) ^ ((uint64_t)a.n_heads << 28) ^
+                         ((uint64_t)a.n_kv << 16) ^ ((uint64_t)head_dim << 6) ^
+                         ((uint64_t)a.max_splits * 0x9E3779B97F4A7C15ull);
+    bool changed;
+    {
+        std::lock_guard<std::mutex> lock(g_layout_mu);
+        if (!g_layout) g_layout = new std::unordered_map<const void*, uint64_t>();
+        auto it = g_layout->find(ws);
+        changed = it == g_layout->end() || it->second != sig;
+        (*g_layout)[ws] = sig;
+    }
+    if (!changed) return ANE_CUDA_OK;
+    const cudaError_t e = cudaMemsetAsync(a.counters, 0, (size_t)batch * a.n_kv * 4, s);
+    if (e != cudaSuccess) return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
+    return ANE_CUDA_OK;
+}
+
 }  // namespace
 
 // Checks shared by the decode-attention entry points; fills `a` except the
@@ -199,6 +227,8 @@ int ane_cuda_decode_attention(int dtype, void* out, int64_t out_stride, const vo
             if (st) return st;
         }
         attention_bind_workspace(&a, workspace, batch, head_dim);
+        st = clear_counters_on_layout_change(a, workspace, batch, head_dim, s);
+        if (st) return st;
     }
     return attention_launch(dtype, a, batch, head_dim, s);
 }

@@ -257,7 +257,9 @@ ANE_CUDA_API int ane_cuda_ane_unpack(float* out, int64_t out_stride, const uint1
  * 16-byte aligned with strides that keep rows 16-byte aligned.
  * Workspace: ane_cuda_decode_attention_workspace_size() bytes (0 when
  * max_len <= 64), 256-byte aligned, zero-filled before its first use (calls
- * leave it zeroed); calls that share one must be ordered on one stream.
+ * leave it zeroed; a call whose shape differs from the previous call's on
+ * the same workspace clears its split counters on the stream first); calls
+ * that share one must be ordered on one stream.
  * workspace == NULL uses a buffer the library allocates per device and
  * stream on first use and keeps. */
 ANE_CUDA_API int64_t ane_cuda_decode_attention_workspace_size(int64_t batch, int n_heads,

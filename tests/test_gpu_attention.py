@@ -172,6 +172,27 @@ def test_attention_caller_workspace_two_calls(ane, oracle):
     assert np.array_equal(bits(got), bits(want))
 
 
+def test_attention_workspace_reused_across_shapes(ane, oracle):
+    """One workspace (the caller's, then the library's own) serving calls of
+    different shapes in turn: a small batch writes split partials where the
+    next, larger batch keeps its split counters.  Every call must still give
+    the oracle's bits."""
+    torch = _torch()
+    rng = np.random.default_rng(77)
+    cases = [(1, 16, 8, 128, 4096, [9], [4096]),
+             (16, 32, 8, 128, 1024, list(rng.integers(0, 1024, 16)), list(rng.integers(1, 1025, 16))),
+             (2, 16, 8, 128, 2048, [100, 7], [2048, 1500]),
+             (16, 32, 8, 128, 1024, list(rng.integers(0, 1024, 16)), list(rng.integers(1, 1025, 16)))]
+    size = max(ane.decode_attention_workspace_size(B, H, hk, hd, cap) for B, H, hk, hd, cap, _, _ in cases)
+    ws = torch.zeros(size, dtype=torch.uint8, device="cuda")
+    for workspace in (ws, None):
+        for B, H, hk, hd, cap, starts, lens in cases:
+            q, k, v, st, ln = make_case(rng, B, H, hk, hd, cap, starts, lens, "f32")
+            want = oracle.decode_attention(q, k, v, st, ln)
+            got = run_gpu(ane, q, k, v, st, ln, "f32", workspace=workspace)
+            assert np.array_equal(bits(got), bits(want)), (B, H, cap, workspace is None)
+
+
 def test_attention_max_len_sizes_launch(ane, oracle):
     """max_len below the capacity launches fewer splits; same bits."""
     rng = np.random.default_rng(12)
