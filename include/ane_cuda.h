@@ -12,7 +12,9 @@
  *   - The return value is an ane_cuda_status; ane_cuda_last_error() gives a
  *     one-line description of the calling thread's last failure.
  *   - Re-entrant: no call keeps state between calls except the per-device
- *     status word read by ane_cuda_read_status_flags().
+ *     status word read by ane_cuda_read_status_flags() and, for decode
+ *     attention, the library-held workspaces and the shape last used with
+ *     each workspace.
  *
  * Reference citations are file:line in the ANE-LM source tree.
  */
