@@ -1,13 +1,17 @@
 """Multi-rank host logic of bench.py on the CPU, as gloo ranks (world size 2).
 
-The layer-op path shards by rows with no collective on the data path: each
-rank owns a disjoint block of global rows and generates its inputs from the
-seed and its row offset.  Checked here: the blocks tile the global rows;
-results computed rank by rank (by the oracle, standing in for the kernels on
-a machine without a GPU) equal one single-process run over all the rows;
-the timing collective returns the slowest rank's time on every rank; the
-whole-job figure counts every rank's rows; the reference arm runs on rank 0
-only.  The gather below is test scaffolding, not part of the path."""
+The layer-op path shards by rows with no collective on the data path: the
+fixed global batch is split into contiguous blocks (sizes differing by at
+most one), and each rank generates its block's inputs from per-sequence
+seeds, so the global inputs do not depend on the number of ranks.  Checked
+here, with an uneven split (13 rows over 2 ranks, sequences of 4 rows that
+straddle the rank boundary): the blocks tile the global rows; each rank's
+inputs equal the matching rows of a single-process batch; results computed
+rank by rank (by the oracle, standing in for the kernels on a machine
+without a GPU) equal one single-process run over all the rows; the timing
+collective returns the slowest rank's values on every rank; the whole-job
+figure counts the global rows once; the reference arm runs on rank 0 only.
+The gather below is test scaffolding, not part of the path."""
 import contextlib
 import datetime
 import io
@@ -19,7 +23,8 @@ import time
 import numpy as np
 
 WORLD = 2
-ROWS_PER_RANK = 6
+TOTAL = 13
+SEQ = 4
 HIDDEN, NQ, NKV, HD, INTER = 256, 4, 2, 64, 384
 
 
@@ -30,26 +35,18 @@ def _free_port():
 
 
 def block_inputs(bench, row0, n):
-    """A rank's inputs: fp16 rows seeded by bench.chain_seed(row0)."""
-    rng = np.random.default_rng(bench.chain_seed(row0))
-    f16 = lambda *s: rng.standard_normal(s).astype(np.float16)  # noqa: E731
-    return {"x": f16(n, HIDDEN), "d": f16(n, HIDDEN), "qkv": f16(n, (NQ + 2 * NKV) * HD),
-            "gate": f16(n, INTER), "up": f16(n, INTER),
-            "pos": ((row0 + np.arange(n)) % 512).astype(np.int32)}
+    """Rows [row0, row0 + n) of the global batch, as bench.py builds them
+    (torch on the CPU here), converted to numpy."""
+    import torch
+    b = bench.make_chain_inputs(torch, row0, n, HIDDEN, NQ, NKV, HD, INTER, SEQ, device="cpu")
+    return {k: v.numpy() for k, v in b.items()}
 
 
-def chain(oracle, b, w, qw, kw):
-    x, y = oracle.residual_rmsnorm(b["x"], b["d"], w)
-    q = oracle.qk_norm_rope(b["qkv"], NQ, NKV, HD, qw, kw, b["pos"], 1e6)
+def chain(oracle, b):
+    x, y = oracle.residual_rmsnorm(b["x"], b["d"], b["w"])
+    q = oracle.qk_norm_rope(b["qkv"], NQ, NKV, HD, b["qw"], b["kw"], b["pos"], 1e6)
     h = oracle.silu_mul(b["gate"], b["up"])
     return np.concatenate([x, y, q, h], axis=1)
-
-
-def weights():
-    rng = np.random.default_rng(7)
-    return ((1 + 0.1 * rng.standard_normal(HIDDEN)).astype(np.float32),
-            (1 + 0.1 * rng.standard_normal(HD)).astype(np.float32),
-            (1 + 0.1 * rng.standard_normal(HD)).astype(np.float32))
 
 
 def _rank_main(rank, port, out_q):
@@ -64,9 +61,11 @@ def _rank_main(rank, port, out_q):
                             timeout=datetime.timedelta(seconds=60))
     try:
         r, lr, wsz = bench.env_rank()
-        row0, n = bench.rank_rows(r, ROWS_PER_RANK)
-        res = chain(Oracle(), block_inputs(bench, row0, n), *weights())
-        slowest = bench.max_over_ranks(torch, dist, wsz, 1.5 + rank)
+        row0, n = bench.rank_rows(r, wsz, TOTAL)
+        b = block_inputs(bench, row0, n)
+        res = chain(Oracle(), b)
+        slowest = bench.max_over_ranks(torch, dist, wsz, [1.5 + rank, 7.0 - rank])
+        one = bench.max_over_ranks(torch, dist, wsz, 2.0 * (rank + 1))
         # the reference arm: rank 0 alone runs it; other ranks return at once
         quiet = None
         if r != 0:
@@ -76,11 +75,38 @@ def _rank_main(rank, port, out_q):
                 bench.run_reference(None)
             quiet = (buf.getvalue() == "", time.perf_counter() - t0)
         gathered = [None] * WORLD
-        dist.all_gather_object(gathered, (r, lr, wsz, row0, n, res, slowest, quiet))
+        dist.all_gather_object(gathered, (r, lr, wsz, row0, n, b, res, slowest, one, quiet))
         if r == 0:
             out_q.put(gathered)
     finally:
         dist.destroy_process_group()
+
+
+def test_row_blocks_are_contiguous_and_balanced():
+    import bench
+    for total in (1, 7, 13, 256, 32768, bench.CONVERT_PARAMS):
+        for world in (1, 2, 3, 4, 8):
+            spans = [bench.rank_rows(r, world, total) for r in range(world)]
+            assert spans[0][0] == 0
+            assert all(a[0] + a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert spans[-1][0] + spans[-1][1] == total
+            sizes = [n for _, n in spans]
+            assert max(sizes) - min(sizes) <= 1
+    # BASELINE config 3 at 8 GPUs: 4096 rows (8 whole sequences) per rank
+    assert bench.rank_rows(7, 8) == (7 * 4096, 4096)
+
+
+def test_rotation_sets_cover_more_than_l2():
+    import bench
+    for world in (1, 2, 4, 8):
+        _, n = bench.rank_rows(0, world)
+        sb = bench.chain_set_bytes(n, bench.HIDDEN, bench.NQ, bench.NKV, bench.HD, bench.INTER)
+        k = bench.rotation_sets(sb)
+        assert k * sb >= bench.ROTATE_BYTES
+        # between two launches of one kernel on one set, the other sets and
+        # kernels stream more than 4 L2s
+        reuse = k * n * bench.B_ROW - n * max(bench.B_NORM, bench.B_QK, bench.B_SILU)
+        assert reuse > 4 * 126e6
 
 
 def test_two_gloo_ranks_shard_rows_without_a_data_path_collective():
@@ -102,20 +128,25 @@ def test_two_gloo_ranks_shard_rows_without_a_data_path_collective():
     from oracle_lib import Oracle
     # rank identity from the launcher's environment
     assert [(g[0], g[1], g[2]) for g in got] == [(r, r, WORLD) for r in range(WORLD)]
-    # disjoint blocks that tile rows [0, WORLD * R)
+    # uneven contiguous blocks that tile rows [0, TOTAL)
     spans = [(g[3], g[4]) for g in got]
-    assert spans == [(r * ROWS_PER_RANK, ROWS_PER_RANK) for r in range(WORLD)]
+    assert spans == [(0, 6), (6, 7)]
+    # each rank's inputs are the matching rows of the single-process batch
+    whole = block_inputs(bench, 0, TOTAL)
+    for (r0, n), g in zip(spans, got):
+        for k in ("x", "d", "qkv", "gate", "up", "pos"):
+            assert np.array_equal(g[5][k], whole[k][r0:r0 + n]), k
+        for k in ("w", "qw", "kw"):
+            assert np.array_equal(g[5][k], whole[k]), k
     # per-rank results == one run over all rows (rows are independent)
-    allb = [block_inputs(bench, r0, n) for r0, n in spans]
-    merged = {k: np.concatenate([b[k] for b in allb]) for k in allb[0]}
-    want = chain(Oracle(), merged, *weights())
-    have = np.concatenate([g[5] for g in got])
+    want = chain(Oracle(), whole)
+    have = np.concatenate([g[6] for g in got])
     assert np.array_equal(have.view(np.uint16), want.view(np.uint16))
-    # the timing collective: the slowest rank's value on every rank
-    assert all(g[6] == 1.5 + (WORLD - 1) for g in got)
-    # whole-job throughput counts every rank's rows over the slowest time
-    one = bench.aggregate_gbs(1, bench.ROWS, 1.0)
-    assert abs(bench.aggregate_gbs(WORLD, bench.ROWS, 1.0) - WORLD * one) < 1e-9
+    # the timing collective: the slowest rank's values on every rank
+    assert all(g[7] == [2.5, 7.0] for g in got)
+    assert all(g[8] == 4.0 for g in got)
+    # whole-job throughput counts the global rows once, over the slowest time
+    assert abs(bench.aggregate_gbs(bench.ROWS, 1.0) - bench.ROWS * bench.B_ROW / 1e6) < 1e-6
     # the reference arm printed nothing on rank 1 and returned at once
-    quiet, dt = got[1][7]
+    quiet, dt = got[1][9]
     assert quiet and dt < 1.0
