@@ -247,8 +247,8 @@ def decode_attention(q, k_cache, v_cache, cache_start, cache_len, max_len=None, 
                      workspace=None):
     """q [batch, n_heads, head_dim]; k_cache, v_cache [batch, capacity, n_kv, head_dim];
     cache_start, cache_len int32 [batch].  Returns out [batch, n_heads, head_dim].
-    workspace: a zero-filled uint8 tensor of decode_attention_workspace_size() bytes,
-    or None for the library-held one."""
+    workspace: a uint8 tensor of decode_attention_workspace_size() bytes (any
+    contents; only the call in flight uses it), or None for the library-held one."""
     torch = _torch()
     _cuda(q, k_cache, v_cache, cache_start, cache_len, workspace)
     batch, n_heads, head_dim = q.shape

@@ -5,6 +5,8 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
+#include <vector>
 
 namespace ane_lm {
 namespace cuda {
@@ -20,14 +22,22 @@ int note(const char* fn, int st) {
     return st;
 }
 
-// Per-thread device staging for sample_token: history ids, the uniform and
-// the result.  Grown on demand, kept for the thread's lifetime.
+// Per-thread device staging for sample_token, one fixed-size block per
+// device: [0] the result, [4] the uniform, [8] the window length, [16..]
+// the window of at most kStageWindow ids.  Only the last
+// repetition_context_size ids of the history are read by the reference
+// (core/sampling.cpp:17-27) and the kernel takes windows up to
+// kStageWindow, so the block never grows: allocated by the thread's first
+// call on a device, freed when the thread exits.
+constexpr int kStageWindow = 4096;
+constexpr int kStageHeader = 4;  // int32 slots before the window
+constexpr int kMaxDevices = 64;
 struct SampleStage {
-    int device = -1;
-    size_t cap = 0;
-    unsigned char* dev = nullptr;
+    int32_t* dev[kMaxDevices] = {};
+    std::vector<int32_t> host;  // the same layout, staged for one copy
     ~SampleStage() {
-        if (dev) cudaFree(dev);
+        for (int d = 0; d < kMaxDevices; d++)
+            if (dev[d]) cudaFree(dev[d]);
     }
 };
 thread_local SampleStage t_stage;
@@ -126,46 +136,55 @@ void gqa_attention(float* out, const float* q, const float* k_cache, const float
 int sample_token(const float* logits, int vocab_size, const SamplingParams& params,
                  const std::vector<int>& recent_tokens) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
         note("sample_token", ANE_CUDA_ERR_CUDA);
         return -1;
     }
-    const size_t nh = recent_tokens.size();
-    const size_t need = 64 + nh * sizeof(int32_t);
-    if (t_stage.device != dev || t_stage.cap < need) {
-        if (t_stage.dev) cudaFree(t_stage.dev);
-        t_stage.dev = nullptr;
-        t_stage.cap = 0;
-        size_t cap = need < 4096 ? 4096 : need * 2;
-        if (cudaMalloc(&t_stage.dev, cap) != cudaSuccess) {
-            fprintf(stderr, "ane_lm::cuda::sample_token: cudaMalloc of %zu bytes failed\n", cap);
+    // the window the reference counts: ids [max(0, n - ctx), n)
+    const int64_t n = (int64_t)recent_tokens.size();
+    const int64_t ctx = params.repetition_context_size > 0 ? params.repetition_context_size : 0;
+    const int64_t w0 = n - ctx > 0 ? n - ctx : 0;
+    const int64_t wn = n - w0;
+    if (wn > kStageWindow) {
+        fprintf(stderr, "ane_lm::cuda::sample_token: repetition window %lld > %d\n", (long long)wn,
+                kStageWindow);
+        t_status = ANE_CUDA_ERR_UNSUPPORTED;
+        return -1;
+    }
+    int32_t*& d_stage = t_stage.dev[dev];
+    if (!d_stage) {
+        const size_t bytes = (size_t)(kStageHeader + kStageWindow) * sizeof(int32_t);
+        if (cudaMalloc(&d_stage, bytes) != cudaSuccess) {
+            fprintf(stderr, "ane_lm::cuda::sample_token: cudaMalloc of %zu bytes failed\n", bytes);
+            d_stage = nullptr;
             t_status = ANE_CUDA_ERR_CUDA;
             return -1;
         }
-        t_stage.device = dev;
-        t_stage.cap = cap;
     }
-    cudaStream_t s = static_cast<cudaStream_t>(t_stream);
-    int32_t* d_out = reinterpret_cast<int32_t*>(t_stage.dev);
-    float* d_u = reinterpret_cast<float*>(t_stage.dev + 16);
-    int32_t* d_len = reinterpret_cast<int32_t*>(t_stage.dev + 32);
-    int32_t* d_hist = reinterpret_cast<int32_t*>(t_stage.dev + 64);
     // the reference draws only when it samples (core/sampling.cpp:45-58)
     const float r = params.temperature > 0.0f ? (float)drand48() : 0.0f;
-    const int32_t len = (int32_t)nh;
-    cudaError_t e = cudaMemcpyAsync(d_u, &r, sizeof(r), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d_len, &len, sizeof(len), cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess && nh)
-        e = cudaMemcpyAsync(d_hist, recent_tokens.data(), nh * sizeof(int32_t),
-                            cudaMemcpyHostToDevice, s);
+    std::vector<int32_t>& h = t_stage.host;
+    h.resize((size_t)(kStageHeader + wn));
+    h[0] = -1;
+    memcpy(&h[1], &r, sizeof(r));
+    h[2] = (int32_t)wn;
+    h[3] = 0;
+    for (int64_t j = 0; j < wn; j++) h[(size_t)(kStageHeader + j)] = recent_tokens[(size_t)(w0 + j)];
+    cudaStream_t s = static_cast<cudaStream_t>(t_stream);
+    cudaError_t e = cudaMemcpyAsync(d_stage, h.data(), h.size() * sizeof(int32_t),
+                                    cudaMemcpyHostToDevice, s);
     if (e != cudaSuccess) {
         fprintf(stderr, "ane_lm::cuda::sample_token: %s\n", cudaGetErrorString(e));
         t_status = ANE_CUDA_ERR_CUDA;
         return -1;
     }
-    int st = ane_cuda_sample_rows(logits, 1, vocab_size, vocab_size, nh ? d_hist : nullptr,
-                                  nh ? d_len : nullptr, (int64_t)nh, d_u, params.temperature,
-                                  params.repetition_penalty, params.repetition_context_size,
+    int32_t* d_out = d_stage;
+    const float* d_u = reinterpret_cast<const float*>(d_stage + 1);
+    const int32_t* d_len = d_stage + 2;
+    const int32_t* d_hist = d_stage + kStageHeader;
+    int st = ane_cuda_sample_rows(logits, 1, vocab_size, vocab_size, wn ? d_hist : nullptr,
+                                  wn ? d_len : nullptr, wn, d_u, params.temperature,
+                                  params.repetition_penalty, (int)(wn ? wn : 0),
                                   params.frequency_penalty, d_out, s);
     if (note("sample_token", st) != ANE_CUDA_OK) return -1;
     int32_t tok = -1;

@@ -3,6 +3,7 @@
 // used when the caller passes none.
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include "attention.cuh"
 
@@ -19,32 +20,39 @@ namespace {
 int64_t round256(int64_t v) { return (v + 255) & ~(int64_t)255; }
 
 struct WsLayout {
-    int64_t counters = 0, ml = 0, o = 0, total = 0;  // byte offsets, total size
+    int64_t ml = 0, o = 0, total = 0;  // byte offsets, total size
 };
 
-// [counters: batch x n_kv u32][m, l: batch x n_heads x splits x 2 f32]
-// [o: batch x n_heads x splits x head_dim f32]; nothing with one split.
-WsLayout ws_layout(int64_t batch, int n_heads, int n_kv, int head_dim, int max_splits) {
+// [m, l: batch x n_heads x splits x 2 f32][o: batch x n_heads x splits x
+// head_dim f32]; nothing with one split.  Only the partials of the call in
+// flight live here: nothing needs to be zero, and nothing is kept between
+// calls.
+WsLayout ws_layout(int64_t batch, int n_heads, int /*n_kv*/, int head_dim, int max_splits) {
     WsLayout w;
     if (max_splits <= 1) return w;
-    w.counters = 0;
-    w.ml = round256(batch * n_kv * 4);
-    w.o = w.ml + round256(batch * n_heads * (int64_t)max_splits * 2 * 4);
+    w.ml = 0;
+    w.o = round256(batch * n_heads * (int64_t)max_splits * 2 * 4);
     w.total = w.o + round256(batch * n_heads * (int64_t)max_splits * head_dim * 4);
     return w;
 }
 
 int splits_of(int max_len) { return max_len <= 0 ? 1 : (max_len + kAttnKeys - 1) / kAttnKeys; }
 
-// Library-held workspace, one per (device, stream): grown with cudaMalloc,
-// zero-filled on allocation (the split counters must start at zero; the
-// kernel leaves them at zero), kept until the process exits.
+// Library-held workspace, one per (device, stream), kept until the process
+// exits.  A buffer is never freed once handed to a kernel: a CUDA graph
+// captured with it may be replayed at any time, so when a larger call needs
+// more, a new buffer is allocated and the old one is kept (retired) too.
+// Allocating is refused while the stream is capturing (a cudaMalloc
+// during a capture can invalidate it, depending on the capture mode):
+// graphs take a caller workspace, or an eager call of the largest shape on
+// the stream comes first.
 struct HeldWs {
     void* ptr = nullptr;
     int64_t bytes = 0;
 };
 std::mutex g_ws_mu;
 std::unordered_map<uint64_t, HeldWs>* g_ws = nullptr;
+std::vector<void*>* g_ws_retired = nullptr;
 
 int held_workspace(cudaStream_t s, int64_t need, void** out) {
     int dev = 0;
@@ -53,56 +61,30 @@ int held_workspace(cudaStream_t s, int64_t need, void** out) {
     const uint64_t key = ((uint64_t)(uintptr_t)s << 8) ^ (uint64_t)dev;
     std::lock_guard<std::mutex> lock(g_ws_mu);
     if (!g_ws) g_ws = new std::unordered_map<uint64_t, HeldWs>();
+    if (!g_ws_retired) g_ws_retired = new std::vector<void*>();
     HeldWs& h = (*g_ws)[key];
     if (h.bytes < need) {
-        if (h.ptr) {
-            e = cudaStreamSynchronize(s);  // the old buffer may still be in use on s
-            if (e == cudaSuccess) e = cudaFree(h.ptr);
-            h.ptr = nullptr;
-            h.bytes = 0;
-            if (e != cudaSuccess)
-                return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
-        }
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(s, &cs);
+        if (e != cudaSuccess)
+            return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
+        if (cs != cudaStreamCaptureStatusNone)
+            return fail(ANE_CUDA_ERR_INVALID_ARG,
+                        "decode_attention: the library-held workspace of this stream must grow to "
+                        "%lld bytes during a stream capture; pass a workspace, or make one eager "
+                        "call of the largest shape on the stream before capturing",
+                        (long long)need);
         const int64_t bytes = need < ((int64_t)1 << 20) ? ((int64_t)1 << 20) : need;
-        e = cudaMalloc(&h.ptr, (size_t)bytes);
-        if (e == cudaSuccess) e = cudaMemsetAsync(h.ptr, 0, (size_t)bytes, s);
-        if (e != cudaSuccess) {
-            if (h.ptr) cudaFree(h.ptr);
-            h.ptr = nullptr;
+        void* p = nullptr;
+        e = cudaMalloc(&p, (size_t)bytes);
+        if (e != cudaSuccess)
             return fail(ANE_CUDA_ERR_CUDA, "decode_attention: workspace of %lld bytes: %s",
                         (long long)bytes, cudaGetErrorString(e));
-        }
+        if (h.ptr) g_ws_retired->push_back(h.ptr);  // a captured graph may still use it
+        h.ptr = p;
         h.bytes = bytes;
     }
     *out = h.ptr;
-    return ANE_CUDA_OK;
-}
-
-// The split counters must read zero when a call starts; every call leaves
-// its own counters at zero.  A call with another layout (batch, heads,
-// head_dim, splits) puts its counters over bytes where the previous call on
-// that workspace kept split partials, so the layout last used with each
-// workspace is remembered and, when it changes, the new counters are
-// cleared on the stream ahead of the kernel.
-std::mutex g_layout_mu;
-std::unordered_map<const void*, uint64_t>* g_layout = nullptr;
-
-int clear_counters_on_layout_change(const AttnArgs& a, const void* ws, int64_t batch,
-                                    int head_dim, cudaStream_t s) {
-    const uint64_t sig = ((uint64_t)batch << 40) ^ ((uint64_t)a.n_heads << 28) ^
-                         ((uint64_t)a.n_kv << 16) ^ ((uint64_t)head_dim << 6) ^
-                         ((uint64_t)a.max_splits * 0x9E3779B97F4A7C15ull);
-    bool changed;
-    {
-        std::lock_guard<std::mutex> lock(g_layout_mu);
-        if (!g_layout) g_layout = new std::unordered_map<const void*, uint64_t>();
-        auto it = g_layout->find(ws);
-        changed = it == g_layout->end() || it->second != sig;
-        (*g_layout)[ws] = sig;
-    }
-    if (!changed) return ANE_CUDA_OK;
-    const cudaError_t e = cudaMemsetAsync(a.counters, 0, (size_t)batch * a.n_kv * 4, s);
-    if (e != cudaSuccess) return fail(ANE_CUDA_ERR_CUDA, "decode_attention: %s", cudaGetErrorString(e));
     return ANE_CUDA_OK;
 }
 
@@ -162,7 +144,6 @@ int attention_args(int dtype, void* out, int64_t out_stride, const void* q, int6
     a->chunks = 1;  // set per launch
     a->stages = 0;
     a->scale = 1.0f / sqrtf((float)head_dim);  // core/cpu_ops.cpp:182
-    a->counters = nullptr;
     a->part_ml = nullptr;
     a->part_o = nullptr;
     a->flags = status_flags_device();
@@ -178,7 +159,6 @@ void attention_bind_workspace(AttnArgs* a, void* ws, int64_t batch, int head_dim
     const WsLayout w = ws_layout(batch, a->n_heads, a->n_kv, head_dim, a->max_splits);
     if (w.total == 0) return;
     unsigned char* base = static_cast<unsigned char*>(ws);
-    a->counters = reinterpret_cast<uint32_t*>(base + w.counters);
     a->part_ml = reinterpret_cast<float*>(base + w.ml);
     a->part_o = reinterpret_cast<float*>(base + w.o);
 }
@@ -227,8 +207,6 @@ int ane_cuda_decode_attention(int dtype, void* out, int64_t out_stride, const vo
             if (st) return st;
         }
         attention_bind_workspace(&a, workspace, batch, head_dim);
-        st = clear_counters_on_layout_change(a, workspace, batch, head_dim, s);
-        if (st) return st;
     }
     return attention_launch(dtype, a, batch, head_dim, s);
 }

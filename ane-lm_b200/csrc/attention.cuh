@@ -12,10 +12,14 @@
 //      on two mbarriers so the score pass starts while V is in flight;
 //   2. computes the scores (a lane group per key, q in registers), the
 //      split's max, exp and sum, and its un-normalised P.V;
-//   3. with one split: writes the output; otherwise writes (m, l, o) to the
-//      workspace, and the CTA that finishes last for its (kv head,
-//      sequence) -- an atomic counter -- combines the splits and writes the
-//      output, then resets the counter to zero.
+//   3. with one split: writes the output; otherwise writes the split's
+//      (m, l, o) to the workspace, and a second kernel (decode_attention_
+//      merge_kernel, launched right behind it with programmatic dependent
+//      launch) combines the splits of each (kv head, sequence) and writes
+//      the output.  No state survives a call: the workspace holds only the
+//      partials of the call in flight, so it needs no clearing, whatever
+//      calls of other shapes, graph replays or interrupted calls used it
+//      before.
 // Every summation order of the fp32 kernel is fixed, so a CPU restatement
 // doing the same operations in the same order reproduces it bit for bit:
 //   dot   EPL = max(16 B / element, head_dim / 32) consecutive elements per
@@ -42,6 +46,7 @@ constexpr int kAttnKeys = 64;  // keys per split (per CTA)
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = kAttnWarps * kWarp;
 constexpr int kAttnMaxGroup = 8;  // q heads per kv head
+constexpr int kAttnMaxDevices = 64;
 static_assert(kAttnThreads == 2 * kAttnKeys, "one copy-issuing thread per K row and per V row");
 
 struct AttnArgs {
@@ -61,7 +66,6 @@ struct AttnArgs {
     int chunks;            // 64-key chunks per CTA (16-bit kernel; 1 for fp32)
     int stages;            // copy stages per warp (16-bit kernel)
     float scale;           // 1 / sqrtf(head_dim)
-    uint32_t* counters;    // [batch][n_kv], zero between calls
     float* part_ml;        // [batch][n_heads][max_splits][2]
     float* part_o;         // [batch][n_heads][max_splits][head_dim]
     unsigned int* flags;   // device status word
@@ -164,25 +168,22 @@ __device__ __forceinline__ void score_block(const typename T::storage* sK,
 // The end of a split, shared by the kernels: s_red holds the four warp
 // partials of P.V ([warp][G][HD]), s_m / s_l the split's max and exp-sum as
 // two halves each.  One split: write the output.  Otherwise write the
-// split's (m, l, o) to the workspace; the CTA that finishes last for its
-// (kv head, sequence) merges the splits and writes the output.
+// split's (m, l, o) to the workspace for decode_attention_merge_kernel.
 template <typename T, int HD, int G>
-__device__ __forceinline__ void attn_finish(const AttnArgs& a, unsigned char* smem, float* s_red,
-                                            float (&s_m)[G][2], float (&s_l)[G][2], float (&s_M)[G],
-                                            float (&s_L)[G][4], int& s_last, int nsplit, int split,
-                                            int kvh, int64_t b, typename T::storage* out) {
-    using S = typename T::storage;
-    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, const float* s_red,
+                                            const float (&s_m)[G][2], const float (&s_l)[G][2],
+                                            int nsplit, int split, int kvh, int64_t b,
+                                            typename T::storage* out) {
+    const int tid = threadIdx.x;
     const int h0 = kvh * G;
-    // the split's o = ((R0 + R1) + R2) + R3 over the warps (or, in the
-    // merge, over the four chains)
+    // the split's o = ((R0 + R1) + R2) + R3 over the warps
     auto sum4 = [&](int g, int d) {
         const float* r = s_red + g * HD + d;
         return __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[G * HD]), r[2 * G * HD]), r[3 * G * HD]);
     };
 
     if (nsplit == 1) {
-        // the merge below with one split: f = exp(m - m), chains 1-3 empty
+        // the merge with one split: f = exp(m - m), chains 1-3 empty
         for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
             const int g = idx / HD, d = idx % HD;
             const float m = fmaxf(s_m[g][0], s_m[g][1]);
@@ -201,116 +202,173 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, unsigned char* sm
         a.part_o[(pbase + (int64_t)g * a.max_splits + split) * HD + d] = sum4(g, d);
     }
     if (tid < G) {
-        float* ml = a.part_ml + (pbase + (int64_t)tid * a.max_splits + split) * 2;
-        ml[0] = fmaxf(s_m[tid][0], s_m[tid][1]);
-        ml[1] = __fadd_rn(s_l[tid][0], s_l[tid][1]);
+        float2* ml = reinterpret_cast<float2*>(a.part_ml) + pbase + (int64_t)tid * a.max_splits + split;
+        *ml = make_float2(fmaxf(s_m[tid][0], s_m[tid][1]), __fadd_rn(s_l[tid][0], s_l[tid][1]));
     }
-    // Release the partials with one fence after the CTA barrier (the barrier
-    // orders every thread's stores before thread 0's fence), count the
-    // split; the last CTA's thread 0 fences again (acquire) and the barrier
-    // passes that on.  One fencing thread instead of 128.
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const uint32_t prev = atomicAdd(a.counters + b * a.n_kv + kvh, 1u);
-        s_last = prev == (uint32_t)(nsplit - 1);
-        if (s_last) {
-            __threadfence();
-            a.counters[b * a.n_kv + kvh] = 0u;  // zero again for the next call
-        }
-    }
-    __syncthreads();
-    if (!s_last) return;
+}
 
-    // ---- 3. merge the splits (last CTA of this kv head and sequence) -------
-    // (m_j, l_j) of up to FT splits at a time in shared memory over the K
-    // rows (no longer needed); M = max m_j; f_j = exp(m_j - M) replaces m_j;
-    // O and L as four fmaf chains over j = c4 (mod 4), in order of j.
-    constexpr int FT = (int)((attn_rows_bytes<T, HD>() / sizeof(float2)) / G) & ~3;
-    constexpr int COLS = HD / 4;
-    constexpr int ITEMS = G * 4 * COLS;  // (g, chain, float4 column)
-    constexpr int IPT = (ITEMS + kAttnThreads - 1) / kAttnThreads;
-    float2* const s_ml = reinterpret_cast<float2*>(smem);  // [G][FT]
-    auto load_ml = [&](int s0, int ns) {
-        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
-            const int g = idx / ns, s = s0 + idx % ns;
-            const float2* ml = reinterpret_cast<const float2*>(a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2);
-            s_ml[g * FT + (s - s0)] = __ldcg(ml + s);
-        }
-    };
-    const bool one_tile = nsplit <= FT;
-    if (one_tile) {
-        load_ml(0, nsplit);
-        __syncthreads();
+// ---- the merge of the splits ------------------------------------------------
+// One CTA per (block of CPB float4 columns of the head dimension, kv head,
+// sequence), serving the G q heads of the kv head.  Launched behind the
+// split kernel with programmatic dependent launch: it is resident and
+// waiting (griddepcontrol.wait) when the last split finishes, and the
+// wait makes every split's partials visible.  The arithmetic is the merge's
+// pinned order: M = max m_j, f_j = exp(m_j - M); O and L each as four fmaf
+// chains over the splits j = c (mod 4), in order of j; the chains added in
+// order; out = O * (1 / L).  Each thread's first PRE partial-o loads are
+// issued before the (m, l) round trip, so the two overlap.
+constexpr int kMergeThreads = 128;
+constexpr int kMergeTile = 256;  // splits per (m, l) tile in shared memory
+
+template <int HD, int G>
+struct MergeShape {
+    static constexpr int COLS = HD / 4;  // float4 columns of a head
+    static constexpr int ALL = G * 4 * COLS;  // (head, chain, column) items of a kv head
+    static constexpr int fp2(int v) { return v >= 2 ? 2 * fp2(v / 2) : 1; }  // power of 2 <= v
+    static constexpr int NB0 = fp2(ALL / kMergeThreads > 0 ? ALL / kMergeThreads : 1);
+    static constexpr int NB = NB0 < COLS ? NB0 : COLS;  // column blocks (CTAs per kv head)
+    static constexpr int CPB = COLS / NB;               // columns per block
+    static constexpr int ITEMS = G * 4 * CPB;
+    static constexpr int IPT = (ITEMS + kMergeThreads - 1) / kMergeThreads;
+    static constexpr int PRE = 16 / IPT;  // partial-o loads issued ahead per item
+    static_assert(COLS % NB == 0 && IPT <= 2, "merge layout");
+};
+
+template <typename T, int HD, int G>
+__global__ void __launch_bounds__(kMergeThreads)
+decode_attention_merge_kernel(const AttnArgs a) {
+    pdl_begin();
+    using MS = MergeShape<HD, G>;
+    constexpr int COLS = MS::COLS, CPB = MS::CPB, ITEMS = MS::ITEMS, IPT = MS::IPT, PRE = MS::PRE;
+    constexpr int FT = kMergeTile;
+    __shared__ float2 s_ml[G][FT];
+    __shared__ float s_M[G], s_L[G][4];
+    __shared__ __align__(16) float s_o[4][G][CPB * 4];
+
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int cb = blockIdx.x, kvh = blockIdx.y;
+    const int64_t b = blockIdx.z;
+    const int len = a.len[b], start = a.start[b];
+    const bool bad = len > a.capacity || len > a.max_len ||
+                     (len > 0 && (start < 0 || start >= a.capacity));
+    if (len <= 0 || bad) return;  // the split kernel wrote zeros
+    const int nchunk = (len + kAttnKeys - 1) / kAttnKeys;
+    const int nsplit = (nchunk + a.chunks - 1) / a.chunks;
+    if (nsplit <= 1) return;  // the split kernel wrote the output
+    const int h0 = kvh * G;
+    const int64_t pbase = (b * a.n_heads + h0) * (int64_t)a.max_splits;
+    const float2* const ml_all = reinterpret_cast<const float2*>(a.part_ml) + pbase;  // [g][max_splits]
+    const float4* const o_all = reinterpret_cast<const float4*>(a.part_o) + pbase * COLS;
+
+    // this thread's items: (head g, chain c4, column col of the block)
+    int it_g[IPT], it_c4[IPT], it_col[IPT];
+    bool it_on[IPT];
+#pragma unroll
+    for (int it = 0; it < IPT; it++) {
+        const int idx = tid + it * kMergeThreads;
+        it_on[it] = ITEMS % kMergeThreads == 0 || idx < ITEMS;
+        const int i = it_on[it] ? idx : 0;
+        it_col[it] = i % CPB;
+        it_c4[it] = (i / CPB) & 3;
+        it_g[it] = i / (4 * CPB);
     }
-    for (int g = w; g < G; g += kAttnWarps) {
-        float mx = -INFINITY;
-        if (one_tile) {
-            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, s_ml[g * FT + s].x);
-        } else {
-            const float* ml = a.part_ml + (pbase + (int64_t)g * a.max_splits) * 2;
-            for (int s = lane; s < nsplit; s += kWarp) mx = fmaxf(mx, __ldcg(ml + 2 * s));
+    auto o_ptr = [&](int it) {  // partial o of split 0 of this item's head and column
+        return o_all + (int64_t)it_g[it] * a.max_splits * COLS + cb * CPB + it_col[it];
+    };
+    const int ns0 = min(nsplit, FT);
+    float4 pre[IPT][PRE];
+#pragma unroll
+    for (int it = 0; it < IPT; it++) {
+        const float4* po = o_ptr(it);
+#pragma unroll
+        for (int r = 0; r < PRE; r++) {
+            const int s = it_c4[it] + 4 * r;
+            if (it_on[it] && s < ns0) pre[it][r] = __ldcg(po + (int64_t)s * COLS);
         }
+    }
+
+    // M = max over all splits; the first tile's (m, l) kept in shared memory
+    for (int idx = tid; idx < G * ns0; idx += kMergeThreads) {
+        const int g = idx / ns0, s = idx % ns0;
+        s_ml[g][s] = __ldcg(ml_all + (int64_t)g * a.max_splits + s);
+    }
+    __syncthreads();
+    for (int g = w; g < G; g += kMergeThreads / kWarp) {
+        float mx = -INFINITY;
+        for (int s = lane; s < ns0; s += kWarp) mx = fmaxf(mx, s_ml[g][s].x);
+        for (int s = FT + lane; s < nsplit; s += kWarp)
+            mx = fmaxf(mx, __ldcg(ml_all + (int64_t)g * a.max_splits + s).x);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
         if (lane == 0) s_M[g] = mx;
     }
+    __syncthreads();
+
     float4 o[IPT];
 #pragma unroll
     for (int it = 0; it < IPT; it++) o[it] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     float Lc = 0.0f;
     for (int s0 = 0; s0 < nsplit; s0 += FT) {
         const int s1 = min(nsplit, s0 + FT), ns = s1 - s0;
-        __syncthreads();  // s_M ready / the previous tile consumed
-        if (!one_tile) {
-            load_ml(s0, ns);
+        if (s0 > 0) {
+            __syncthreads();  // the previous tile consumed
+            for (int idx = tid; idx < G * ns; idx += kMergeThreads) {
+                const int g = idx / ns, s = idx % ns;
+                s_ml[g][s] = __ldcg(ml_all + (int64_t)g * a.max_splits + s0 + s);
+            }
             __syncthreads();
         }
-        for (int idx = tid; idx < G * ns; idx += kAttnThreads) {
-            float2& e = s_ml[(idx / ns) * FT + idx % ns];
+        for (int idx = tid; idx < G * ns; idx += kMergeThreads) {
+            float2& e = s_ml[idx / ns][idx % ns];
             e.x = pinned_expf(__fsub_rn(e.x, s_M[idx / ns]));
         }
         __syncthreads();
 #pragma unroll
         for (int it = 0; it < IPT; it++) {
-            const int idx = tid + it * kAttnThreads;
-            if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
-                const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
-                const float4* po =
-                    reinterpret_cast<const float4*>(a.part_o + (pbase + (int64_t)g * a.max_splits) * HD) + col;
-                const float2* f = s_ml + g * FT - s0;
-#pragma unroll 16
-                for (int s = s0 + c4; s < s1; s += 4) {
-                    const float4 v = __ldcg(po + (int64_t)s * COLS);
-                    const float fs = f[s].x;
-                    o[it].x = __fmaf_rn(v.x, fs, o[it].x);
-                    o[it].y = __fmaf_rn(v.y, fs, o[it].y);
-                    o[it].z = __fmaf_rn(v.z, fs, o[it].z);
-                    o[it].w = __fmaf_rn(v.w, fs, o[it].w);
+            if (!it_on[it]) continue;
+            const float2* f = s_ml[it_g[it]] - s0;
+            int s = s0 + it_c4[it];
+            if (s0 == 0) {
+#pragma unroll
+                for (int r = 0; r < PRE; r++, s += 4) {
+                    if (s < s1) {
+                        const float fs = f[s].x;
+                        o[it].x = __fmaf_rn(pre[it][r].x, fs, o[it].x);
+                        o[it].y = __fmaf_rn(pre[it][r].y, fs, o[it].y);
+                        o[it].z = __fmaf_rn(pre[it][r].z, fs, o[it].z);
+                        o[it].w = __fmaf_rn(pre[it][r].w, fs, o[it].w);
+                    }
                 }
+            }
+            const float4* po = o_ptr(it);
+#pragma unroll 16
+            for (; s < s1; s += 4) {
+                const float4 v = __ldcg(po + (int64_t)s * COLS);
+                const float fs = f[s].x;
+                o[it].x = __fmaf_rn(v.x, fs, o[it].x);
+                o[it].y = __fmaf_rn(v.y, fs, o[it].y);
+                o[it].z = __fmaf_rn(v.z, fs, o[it].z);
+                o[it].w = __fmaf_rn(v.w, fs, o[it].w);
             }
         }
         if (tid < 4 * G) {
             const int c4 = tid & 3, g = tid >> 2;
-            const float2* f = s_ml + g * FT - s0;
+            const float2* f = s_ml[g] - s0;
             for (int s = s0 + c4; s < s1; s += 4) Lc = __fmaf_rn(f[s].y, f[s].x, Lc);
         }
     }
-    __syncthreads();  // the chains are in registers; s_red reuses the (m, l) tile
 #pragma unroll
-    for (int it = 0; it < IPT; it++) {
-        const int idx = tid + it * kAttnThreads;
-        if (ITEMS % kAttnThreads == 0 || idx < ITEMS) {
-            const int col = idx % COLS, c4 = (idx / COLS) & 3, g = idx / (4 * COLS);
-            reinterpret_cast<float4*>(s_red + (c4 * G + g) * HD)[col] = o[it];
-        }
-    }
+    for (int it = 0; it < IPT; it++)
+        if (it_on[it]) reinterpret_cast<float4*>(s_o[it_c4[it]][it_g[it]])[it_col[it]] = o[it];
     if (tid < 4 * G) s_L[tid >> 2][tid & 3] = Lc;
     __syncthreads();
-    for (int idx = tid; idx < G * HD; idx += kAttnThreads) {
-        const int g = idx / HD, d = idx % HD;
+    typename T::storage* const out =
+        static_cast<typename T::storage*>(a.out) + b * a.out_stride + (int64_t)h0 * HD + cb * CPB * 4;
+    for (int idx = tid; idx < G * CPB * 4; idx += kMergeThreads) {
+        const int g = idx / (CPB * 4), d = idx % (CPB * 4);
         const float L = __fadd_rn(__fadd_rn(__fadd_rn(s_L[g][0], s_L[g][1]), s_L[g][2]), s_L[g][3]);
-        out[idx] = T::from_f(__fmul_rn(sum4(g, d), __fdiv_rn(1.0f, L)));
+        const float O = __fadd_rn(__fadd_rn(__fadd_rn(s_o[0][g][d], s_o[1][g][d]), s_o[2][g][d]), s_o[3][g][d]);
+        out[(int64_t)g * HD + d] = T::from_f(__fmul_rn(O, __fdiv_rn(1.0f, L)));
     }
 }
 
@@ -332,8 +390,7 @@ decode_attention_kernel(const AttnArgs a) {
     float* const s_p = reinterpret_cast<float*>(smem + attn_rows_bytes<T, HD>());  // [key][PROW]
     float* const s_red = reinterpret_cast<float*>(smem);  // [warp][G][HD], over the K rows
     __shared__ __align__(8) uint64_t bars[2];
-    __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
-    __shared__ int s_last;
+    __shared__ float s_m[G][2], s_l[G][2];
 
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int split = blockIdx.x, kvh = blockIdx.y;
@@ -414,8 +471,16 @@ decode_attention_kernel(const AttnArgs a) {
         for (int c = 0; c < NV; c++) unpack<T>(ld_keep(qp + c * V), &qf[g][c * V]);
     }
 
-    if (!__syncthreads_and(mbar_wait_bounded(&bars[0], 0))) {
+    // A wait that gives up raises the flag, waits once more (bounded) for
+    // the CTA's copies still in flight into its shared memory, and leaves
+    // without output; the flag marks the call's results as invalid.
+    auto give_up = [&]() {
         if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+        mbar_wait_bounded(&bars[0], 0);
+        if constexpr (!VREG) mbar_wait_bounded(&bars[1], 0);
+    };
+    if (!__syncthreads_and(mbar_wait_bounded(&bars[0], 0))) {
+        give_up();
         return;
     }
 
@@ -448,7 +513,7 @@ decode_attention_kernel(const AttnArgs a) {
     if constexpr (VREG) {
         __syncthreads();
     } else if (!__syncthreads_and(mbar_wait_bounded(&bars[1], 0))) {
-        if (tid == 0 && a.flags) atomicOr(a.flags, ANE_CUDA_FLAG_WAIT_TIMEOUT);
+        give_up();
         return;
     }
 
@@ -505,7 +570,7 @@ decode_attention_kernel(const AttnArgs a) {
     }
     __syncthreads();
 
-    attn_finish<T, HD, G>(a, smem, s_red, s_m, s_l, s_M, s_L, s_last, nsplit, split, kvh, b, out);
+    attn_finish<T, HD, G>(a, s_red, s_m, s_l, nsplit, split, kvh, b, out);
 }
 
 
@@ -535,9 +600,10 @@ decode_attention_kernel(const AttnArgs a) {
 // max m, sum l and o per head (online softmax: when m grows, l and o are
 // scaled by exp(m_old - m_new)); at the end the four warps are merged with
 // f_w = exp(m_w - M) into the split's (M, L, O), which attn_finish writes
-// or merges like the fp32 kernel's.  The summation orders differ from the
-// fp32 kernel's (the MMA's internal order is the hardware's): results
-// agree with the fp32 order to within the output type's rounding.
+// out, or leaves for the merge kernel, like the fp32 kernel's.  The
+// summation orders differ from the fp32 kernel's (the MMA's internal order
+// is the hardware's): results agree with the fp32 order to within the
+// output type's rounding.
 // K and V rows sit in shared memory with a 16-byte pad per row, which makes
 // the fragment loads (ldmatrix for K, ldmatrix.trans for V) free of bank
 // conflicts.
@@ -631,15 +697,13 @@ decode_attention_mma_kernel(const AttnArgs a) {
     constexpr bool F16S = std::is_same<T, F16>::value;
     constexpr float PSCALE = F16S ? 4096.0f : 1.0f;  // 2^12: fp16 low parts stay normal
     static_assert(WK == 16, "one 16-deep k-step of P.V per warp and chunk");
-    // the warp partials and the merge tile of attn_finish fit in one stage set
+    // the warp partials fit in one stage set
     static_assert((size_t)kAttnWarps * G * HD * sizeof(float) <= attn_mma_smem_bytes<HD>(1),
                   "warp partials");
-    static_assert(attn_rows_bytes<T, HD>() <= attn_mma_smem_bytes<HD>(1), "merge tile");
     extern __shared__ __align__(16) unsigned char smem[];
     float* const s_red = reinterpret_cast<float*>(smem);  // [warp][G][HD], after the pipelines
-    __shared__ float s_m[G][2], s_l[G][2], s_M[G], s_L[G][4];
+    __shared__ float s_m[G][2], s_l[G][2];
     __shared__ float s_wm[G][kAttnWarps], s_wl[G][kAttnWarps];
-    __shared__ int s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int gid = lane >> 2, tq = lane & 3;  // MMA fragment row / column pair
@@ -877,7 +941,7 @@ decode_attention_mma_kernel(const AttnArgs a) {
         s_l[tid][1] = __fadd_rn(lw[2], lw[3]);
     }
     __syncthreads();
-    attn_finish<T, HD, G>(a, smem, s_red, s_m, s_l, s_M, s_L, s_last, nsplit, split, kvh, b, out);
+    attn_finish<T, HD, G>(a, s_red, s_m, s_l, nsplit, split, kvh, b, out);
 }
 
 // Launches the kernel instance for (head_dim, group); ANE_CUDA_ERR_UNSUPPORTED
@@ -902,9 +966,14 @@ int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
         constexpr int smax = attn_mma_max_stages<HD>();
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)attn_mma_smem_bytes<HD>(smax));
-        // CTAs resident per SM with rings of 1 .. smax stages (the same on
-        // every device of a process: queried once)
-        static std::atomic<int> occ[kAttnMaxStages + 1];
+        // CTAs resident per SM with rings of 1 .. smax stages, queried once
+        // per device
+        static std::atomic<int> occ_dev[kAttnMaxDevices][kAttnMaxStages + 1];
+        int dev = 0;
+        if (e == cudaSuccess) e = cudaGetDevice(&dev);
+        if (e == cudaSuccess && (dev < 0 || dev >= kAttnMaxDevices))
+            return fail(ANE_CUDA_ERR_UNSUPPORTED, "decode_attention: device %d", dev);
+        std::atomic<int>* const occ = occ_dev[dev];
         for (int st = 1; st <= smax && e == cudaSuccess; st++) {
             if (occ[st].load(std::memory_order_relaxed) > 0) continue;
             int per_sm = 0;
@@ -964,6 +1033,10 @@ int launch_attention_shape(const AttnArgs& a, int64_t batch, cudaStream_t s) {
     }
     const dim3 grid(gx, (unsigned)a.n_kv, (unsigned)batch);
     launch_pdl(kern, grid, kAttnThreads, smem, s, la);
+    if (gx > 1) {  // some (kv head, sequence) may have several splits
+        const dim3 mgrid((unsigned)MergeShape<HD, G>::NB, (unsigned)a.n_kv, (unsigned)batch);
+        launch_pdl(decode_attention_merge_kernel<T, HD, G>, mgrid, kMergeThreads, 0, s, la);
+    }
     return check_launch("decode_attention");
 }
 

@@ -20,9 +20,9 @@
 
 namespace ane {
 
-// split counters + per-split (m, l, o) for at most this many bytes: enough
-// for one sequence of 32K keys with 32 q heads of 128 (Qwen3-8B decode), or
-// 64 sequences of 1K keys.
+// per-split (m, l, o) for at most this many bytes: enough for one sequence
+// of 32K keys with 32 q heads of 128 (Qwen3-8B decode), or 64 sequences of
+// 1K keys.
 constexpr int64_t kStaticScratchBytes = (int64_t)16 << 20;
 
 static __device__ __align__(256) unsigned char g_attn_scratch[kStaticScratchBytes];
@@ -41,29 +41,39 @@ int attention_launch(int dtype, const AttnArgs& a, int64_t batch, int head_dim, 
 namespace {
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_scratch_once[kMaxDevices];
+std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices];
 
-// The array's device address on the current device, looked up once per
-// device, by the first call made with that device current (the lookup is
-// a runtime call of its own: that first call belongs before any stream
-// capture on the device).
-int static_scratch(void** out) {
+// The array's device address on the current device, looked up by the first
+// call made with that device current and kept once the lookup succeeds (a
+// failed lookup is tried again by the next call).  The lookup is a runtime
+// call of its own, so that first call belongs before any stream capture on
+// the device: a call that would look the address up while `s` is capturing
+// is refused instead.
+int static_scratch(cudaStream_t s, void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess)
         return fail(ANE_CUDA_ERR_CUDA, "decode_attention_static: %s", cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices)
         return fail(ANE_CUDA_ERR_UNSUPPORTED, "decode_attention_static: device %d", dev);
-    std::call_once(g_scratch_once[dev], [dev] {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev]) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(s, &cs);
+        if (e != cudaSuccess)
+            return fail(ANE_CUDA_ERR_CUDA, "decode_attention_static: %s", cudaGetErrorString(e));
+        if (cs != cudaStreamCaptureStatusNone)
+            return fail(ANE_CUDA_ERR_INVALID_ARG,
+                        "decode_attention_static: first call on device %d during a stream "
+                        "capture; make one call on the device before capturing", dev);
         void* p = nullptr;
-        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_attn_scratch);
+        e = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(ANE_CUDA_ERR_CUDA, "decode_attention_static: scratch address: %s",
+                        cudaGetErrorString(e));
         g_scratch_addr[dev] = p;
-    });
-    if (g_scratch_err[dev] != cudaSuccess || !g_scratch_addr[dev])
-        return fail(ANE_CUDA_ERR_CUDA, "decode_attention_static: scratch address: %s",
-                    cudaGetErrorString(g_scratch_err[dev]));
+    }
     *out = g_scratch_addr[dev];
     return ANE_CUDA_OK;
 }
@@ -97,15 +107,9 @@ int ane_cuda_decode_attention_static(int dtype, void* out, int64_t out_stride, c
     const cudaStream_t s = as_stream(stream);
     if (need > 0) {
         void* scratch = nullptr;
-        st = static_scratch(&scratch);
+        st = static_scratch(s, &scratch);
         if (st) return st;
         attention_bind_workspace(&a, scratch, batch, head_dim);
-        // The split counters must read zero when the kernel starts.  Calls
-        // leave them at zero, but a call cut short (an error in between)
-        // may not: clear them on the stream, ahead of the kernel.
-        const cudaError_t e = cudaMemsetAsync(a.counters, 0, (size_t)batch * n_kv_heads * 4, s);
-        if (e != cudaSuccess)
-            return fail(ANE_CUDA_ERR_CUDA, "decode_attention_static: %s", cudaGetErrorString(e));
     }
     return attention_launch(dtype, a, batch, head_dim, s);
 }

@@ -1,4 +1,5 @@
 // capi.cu -- status reporting and the per-device status word of the C ABI.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -24,17 +25,19 @@ int check_launch(const char* what) {
     return ANE_CUDA_OK;
 }
 
+// Cached per device; concurrent first calls from several host threads each
+// store the same value (atomics, so there is no data race).
 int sm_count() {
-    static int cache[64] = {0};
+    static std::atomic<int> cache[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-    if (cache[dev] == 0) {
-        int n = 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
+    if (n == 0) {
         if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
             n = 148;
-        cache[dev] = n;
+        cache[dev].store(n, std::memory_order_relaxed);
     }
-    return cache[dev];
+    return n;
 }
 
 int resident_grid(const void* kernel, int threads, size_t smem, int64_t want) {

@@ -4,6 +4,8 @@
 // One warp per output row; 16-byte vector copies when the row width and
 // both base pointers allow it, element copies otherwise.  Out-of-range ids
 // write a zero row and raise ANE_CUDA_FLAG_BAD_TOKEN_ID.
+#include <atomic>
+
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
@@ -61,16 +63,20 @@ gather_elem_kernel(typename TO::storage* __restrict__ out,
     for (int c = lane; c < hidden; c += kWarp) o[c] = TO::from_f(TI::to_f(t[c]));
 }
 
+// Looked up once per device (a failed lookup is retried); concurrent first
+// calls store the same address (atomics, so there is no data race).
 unsigned int* status_flags_device() {
-    static unsigned int* addr[64] = {};
+    static std::atomic<unsigned int*> addr[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-    if (!addr[dev]) {
+    unsigned int* a = addr[dev].load(std::memory_order_acquire);
+    if (!a) {
         void* p = nullptr;
         if (cudaGetSymbolAddress(&p, g_status_flags) != cudaSuccess) return nullptr;
-        addr[dev] = static_cast<unsigned int*>(p);
+        a = static_cast<unsigned int*>(p);
+        addr[dev].store(a, std::memory_order_release);
     }
-    return addr[dev];
+    return a;
 }
 
 }  // namespace ane

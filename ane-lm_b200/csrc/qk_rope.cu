@@ -55,6 +55,9 @@ struct QkArgs {
     const int32_t* slots;
     int cache_capacity;        // slots outside [0, capacity) write nothing and raise a flag
     unsigned int* flags;
+    // generic path only: RoPE over interleaved pairs (2j, 2j + 1), the
+    // reference's fallback without tables (core/cpu_ops.cpp:66-77)
+    int interleaved;
 };
 
 // One warp per row.  The row's heads stream through a ring of D register
@@ -272,6 +275,18 @@ qk_norm_rope_generic_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr)
     }
     const int half = a.rot_dim / 2;
     const float fpos = (float)(a.positions ? __ldg(a.positions + row) : a.pos);
+    if (a.interleaved) {
+        // pair (2j, 2j + 1): angle = pos * inv_freq[j], unfused products
+        for (int j = lane; j < half; j += kWarp) {
+            float c, s;
+            pinned_sincosf(__fmul_rn(fpos, fr.f[j]), &s, &c);
+            const float x0 = v[2 * j], x1 = v[2 * j + 1];
+            base[2 * j] = T::from_f(__fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s)));
+            base[2 * j + 1] = T::from_f(__fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c)));
+        }
+        for (int i = a.rot_dim + lane; i < hd; i += kWarp) base[i] = T::from_f(v[i]);
+        return;
+    }
     for (int j = lane; j < half; j += kWarp) {
         float c, s;
         if (a.cos_row) {
@@ -311,7 +326,7 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s, bool k
     const int nh = a.n_q + a.n_kv;
     const int nchunk = a.head_dim / V;
     const int gl_log2 = ilog2_exact(nchunk) - 1;
-    bool fast = a.cos_row == nullptr && a.rot_dim == a.head_dim && a.head_dim % V == 0 &&
+    bool fast = a.cos_row == nullptr && !a.interleaved && a.rot_dim == a.head_dim && a.head_dim % V == 0 &&
                 gl_log2 >= 0 && nchunk <= 32 && is_aligned(a.q, 16) && is_aligned(a.k, 16) &&
                 (a.q_row_stride * es) % 16 == 0 && (a.k_row_stride * es) % 16 == 0 &&
                 (a.q_head_stride * es) % 16 == 0 && (a.k_head_stride * es) % 16 == 0;
@@ -427,8 +442,13 @@ int ane_cuda_apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads
                                float theta, const float* cos_row, const float* sin_row,
                                void* stream) {
     using namespace ane;
+    // core/cpu_ops.cpp:62-77: both tables -> the half-split fast path;
+    // either one NULL -> the fallback over interleaved pairs
+    const bool tables = cos_row != nullptr && sin_row != nullptr;
     QkArgs a{q, k, 0, 0, q_head_stride, k_head_stride, n_q_heads, n_kv_heads, head_dim, rot_dim,
-             nullptr, nullptr, nullptr, pos, 1, 0.0f, cos_row, sin_row};
+             nullptr, nullptr, nullptr, pos, 1, 0.0f, tables ? cos_row : nullptr,
+             tables ? sin_row : nullptr};
+    a.interleaved = tables ? 0 : 1;
     int st = validate("apply_rope_cached", a);
     if (st) return st;
     return run_qk(ANE_CUDA_F32, a, theta, as_stream(stream));

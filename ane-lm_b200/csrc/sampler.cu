@@ -30,6 +30,8 @@
 //         found insignificant stays so.  The exps that are needed are
 //         compacted per warp through shared memory, so a warp evaluates
 //         ceil(significant / 32) exps per slot instead of one per element.
+#include <atomic>
+
 #include "ane_common.cuh"
 #include "ane_internal.h"
 
@@ -270,7 +272,17 @@ sample_rows_kernel(const SampArgs a) {
     const int ngroups = (a.vocab + 3) >> 2;
 
     // ---- greedy: first maximum (core/sampling.cpp:45-52) ----
+    // The reference keeps max_i = 0 and moves on `adjusted[i] >
+    // adjusted[max_i]`: a NaN never wins a comparison, so element 0 being
+    // NaN gives 0, and otherwise the result is the first index of the
+    // largest non-NaN value (element 0 included).
     if (a.temperature <= 0.0f) {
+        float v0[4];
+        load4(a, lrow, P, 0, v0);
+        if (v0[0] != v0[0]) {
+            if (tid == 0) a.out[row] = 0;
+            return;
+        }
         float best = -INFINITY;
         int bi = 0x7FFFFFFF;
         for (int g = tid; g < ngroups; g += kSampThreads) {
@@ -279,7 +291,10 @@ sample_rows_kernel(const SampArgs a) {
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int i = g * 4 + e;
-                if (i < a.vocab && (v[e] > best || bi == 0x7FFFFFFF)) { best = v[e]; bi = i; }
+                if (i < a.vocab && v[e] == v[e] && (v[e] > best || (v[e] == best && i < bi))) {
+                    best = v[e];
+                    bi = i;
+                }
             }
         }
         // larger value wins, equal values -> smaller index
@@ -304,7 +319,10 @@ sample_rows_kernel(const SampArgs a) {
     }
 
     // ---- pass 1: max, four groups in flight per thread ----
+    // fmaxf skips NaN like the reference's `>` scan (vDSP_maxv); NaNs are
+    // counted on the side.
     float mx = -INFINITY;
+    bool nan_seen = false;
     for (int g0 = 0; g0 < ngroups; g0 += 4 * kSampThreads) {
         float v[4][4];
 #pragma unroll
@@ -316,11 +334,25 @@ sample_rows_kernel(const SampArgs a) {
 #pragma unroll
         for (int u = 0; u < 4; u++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) mx = fmaxf(mx, v[u][e]);
+            for (int e = 0; e < 4; e++) {
+                mx = fmaxf(mx, v[u][e]);
+                nan_seen |= v[u][e] != v[u][e];
+            }
     }
+    nan_seen = __syncthreads_or(nan_seen);
     mx = block_max(mx, S);
     const float inv_t = __fdiv_rn(1.0f, a.temperature);
     const float neg_m = -__fmul_rn(mx, inv_t);
+    const float r = __ldg(a.uniforms + row);
+    // The reference's softmax sum is NaN exactly when a penalised logit is
+    // NaN (exp(NaN) = NaN) or max * (1/T) is infinite (+inf - inf, or every
+    // element -inf + inf); then every p is NaN, `cum >= r` never holds and
+    // it returns vocab - 1 (core/sampling.cpp:58-65).  A NaN uniform never
+    // compares true either.
+    if (nan_seen || !(fabsf(neg_m) <= 3.402823466e38f) || r != r) {
+        if (tid == 0) a.out[row] = a.vocab - 1;
+        return;
+    }
 
     // ---- pass 2: pinned sum of exp over the 1024 virtual threads ----
     float acc_lo = 0.0f, acc_hi = 0.0f;
@@ -356,7 +388,6 @@ sample_rows_kernel(const SampArgs a) {
     const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
 
     // ---- pass 3: exact parallel inverse-CDF scan over significant elements ----
-    const float r = __ldg(a.uniforms + row);
     if (!(r > 0.0f)) {  // cum >= r holds after the first element
         if (tid == 0) a.out[row] = 0;
         return;
@@ -643,18 +674,22 @@ softmax_rows_kernel(float* x, int n, int64_t stride) {
     for (int g = tid; g < ngroups; g += kSampThreads)
         for (int e = 0; e < 4 && g * 4 + e < n; e++) mx = fmaxf(mx, row[g * 4 + e]);
     const float neg_m = -block_max(mx, S);
+    // x - max is <= 0 or NaN (a NaN element, +inf - inf, or -inf + inf when
+    // every element is -inf): NaN stays NaN through the exp, as in the
+    // reference's vvexpf, and then makes the sum and every output NaN
+    auto ex = [](float d) { return d != d ? d : pinned_expf_nonpos(d); };
     float acc_lo = 0.0f, acc_hi = 0.0f;
     for (int g0 = 0; g0 < ngroups; g0 += kVirtThreads) {
         const int ga = g0 + tid, gb = g0 + tid + kSampThreads;
         if (ga < ngroups)
             for (int e = 0; e < 4 && ga * 4 + e < n; e++) {
-                const float v = pinned_expf_nonpos(__fadd_rn(row[ga * 4 + e], neg_m));
+                const float v = ex(__fadd_rn(row[ga * 4 + e], neg_m));
                 row[ga * 4 + e] = v;
                 acc_lo = __fadd_rn(acc_lo, v);
             }
         if (gb < ngroups)
             for (int e = 0; e < 4 && gb * 4 + e < n; e++) {
-                const float v = pinned_expf_nonpos(__fadd_rn(row[gb * 4 + e], neg_m));
+                const float v = ex(__fadd_rn(row[gb * 4 + e], neg_m));
                 row[gb * 4 + e] = v;
                 acc_hi = __fadd_rn(acc_hi, v);
             }
@@ -694,16 +729,18 @@ int ane_cuda_sample_rows(const float* logits, int64_t rows, int vocab, int64_t l
     const size_t smem = (size_t)(1 << slots_log2) * 12 + (size_t)((vocab + 31) / 32) * 4;
     constexpr size_t kMaxDyn = 180 * 1024;  // plus 16 KB of static shared memory
     if (smem > kMaxDyn) return fail(ANE_CUDA_ERR_UNSUPPORTED, "sample_rows: vocab %d too large", vocab);
-    static int configured[64] = {0};
+    // the attribute is set once per device (setting it twice is harmless,
+    // so concurrent first calls need no lock)
+    static std::atomic<int> configured[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return fail(ANE_CUDA_ERR_CUDA, "sample_rows: no current device");
-    if (!configured[dev]) {
+    if (!configured[dev].load(std::memory_order_acquire)) {
         cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDyn);
         if (e != cudaSuccess)
             return fail(ANE_CUDA_ERR_CUDA, "sample_rows: %s", cudaGetErrorString(e));
-        configured[dev] = 1;
+        configured[dev].store(1, std::memory_order_release);
     }
     SampArgs a{logits, rows, vocab, logits_stride, history, history_len, history_stride, uniforms,
                temperature, repetition_penalty, frequency_penalty, repetition_context, out_tokens,

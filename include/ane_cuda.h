@@ -151,10 +151,13 @@ ANE_CUDA_API int ane_cuda_qk_norm_rope_kv(int dtype, void* q, void* k, const voi
                                           const int32_t* slots, int cache_capacity, int64_t rows,
                                           float theta, float eps, void* stream);
 
-/* The single-position form with caller-supplied cos/sin rows, exactly
- * apply_rope_cached (core/cpu_ops.h:25-28) on fp32 device data.  When
- * cos_row or sin_row is NULL, cos/sin are computed in registers (half-split
- * layout, the layout of the fast path). */
+/* The single-position form, apply_rope_cached (core/cpu_ops.h:25-28,
+ * core/cpu_ops.cpp:56-80) on fp32 device data.  With both cos_row and
+ * sin_row: the half-split fast path on those tables (:43-54).  When either
+ * is NULL: the reference's on-the-fly fallback (:66-77), which rotates
+ * interleaved pairs (v[2j], v[2j+1]) by angle pos / theta^(2j/rot_dim),
+ * cos/sin computed in registers (within 2 ulp of libm's cosf / sinf at
+ * unit scale).  rot_dim must be even. */
 ANE_CUDA_API int ane_cuda_apply_rope_cached(float* q, float* k, int n_q_heads, int n_kv_heads,
                                int head_dim, int q_head_stride, int k_head_stride,
                                int rot_dim, int pos, float theta, const float* cos_row,
@@ -258,12 +261,16 @@ ANE_CUDA_API int ane_cuda_ane_unpack(float* out, int64_t out_stride, const uint1
  * head_dim 64, 128 or 256; at most 8 q heads per kv head; q and the caches
  * 16-byte aligned with strides that keep rows 16-byte aligned.
  * Workspace: ane_cuda_decode_attention_workspace_size() bytes (0 when
- * max_len <= 64), 256-byte aligned, zero-filled before its first use (calls
- * leave it zeroed; a call whose shape differs from the previous call's on
- * the same workspace clears its split counters on the stream first); calls
- * that share one must be ordered on one stream.
+ * max_len <= 64), 256-byte aligned, any contents: it holds only the split
+ * partials of the call in flight (a second kernel, launched behind the
+ * first, merges them), so nothing is kept between calls and nothing needs
+ * clearing; calls that share one must be ordered on one stream.
  * workspace == NULL uses a buffer the library allocates per device and
- * stream on first use and keeps. */
+ * stream and keeps until exit; when a larger call needs more it allocates
+ * another and keeps the old one too (a captured graph may still use it).
+ * That buffer is never allocated during a stream capture: such a call
+ * returns ANE_CUDA_ERR_INVALID_ARG -- capture with a caller workspace, or
+ * after one eager call of the largest shape on the stream. */
 ANE_CUDA_API int64_t ane_cuda_decode_attention_workspace_size(int64_t batch, int n_heads,
                                                               int n_kv_heads, int head_dim,
                                                               int max_len);
@@ -289,7 +296,8 @@ ANE_CUDA_API int ane_cuda_decode_attention(int dtype, void* out, int64_t out_str
  * device: calls whose executions overlap race on it -- order them on one
  * stream.  The first call on each device looks up the array's device
  * address (cudaGetSymbolAddress, with that device current); make that first
- * call before any stream capture on the device. */
+ * call before any stream capture on the device (a first call made during a
+ * capture returns ANE_CUDA_ERR_INVALID_ARG and leaves the capture intact). */
 ANE_CUDA_API int64_t ane_cuda_decode_attention_static_capacity(void);
 ANE_CUDA_API int ane_cuda_decode_attention_static(int dtype, void* out, int64_t out_stride,
                                                   const void* q, int64_t q_stride,

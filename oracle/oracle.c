@@ -392,6 +392,32 @@ void or_qk_norm_rope(int dt, void* q, void* k, int64_t qrs, int64_t krs,
     free(inv_freq); free(cs); free(sn); free(v);
 }
 
+/* apply_rope_cached without tables: the reference's on-the-fly fallback,
+ * core/cpu_ops.cpp:66-77 (taken when cos_row or sin_row is NULL), on fp32
+ * heads in place: for each pair (i, i+1), i = 2j < rot_dim,
+ *   freq = 1 / powf(theta, i / rot_dim), angle = pos * freq,
+ *   v[i]   = v0 * cos - v1 * sin
+ *   v[i+1] = v0 * sin + v1 * cos                    (unfused)
+ * with powf / cosf / sinf taken as the pinned inv_freq and sincos above. */
+void or_apply_rope_interleaved(float* q, float* k, int nq, int nkv, int qhs, int khs, int rot,
+                               int pos, float theta) {
+    int half = rot / 2;
+    float* inv_freq = (float*)malloc((size_t)(half > 0 ? half : 1) * sizeof(float));
+    or_rope_inv_freq(inv_freq, rot, theta);
+    for (int h = 0; h < nq + nkv; h++) {
+        float* v = h < nq ? q + (int64_t)h * qhs : k + (int64_t)(h - nq) * khs;
+        for (int j = 0; j < half; j++) {
+            float c, s;
+            or_sincosf((float)pos * inv_freq[j], &s, &c);
+            float v0 = v[2 * j], v1 = v[2 * j + 1];
+            float a = v0 * c, b = v1 * s, d = v0 * s, e = v1 * c;
+            v[2 * j] = a - b;
+            v[2 * j + 1] = d + e;
+        }
+    }
+    free(inv_freq);
+}
+
 /* QK-norm + RoPE followed by the KV-cache write of the decode step,
  * models/llm/qwen3.cpp:470-488: after RoPE, the token's k heads and its v
  * heads are copied (memcpy) into ring slot slots[r] of the caches

@@ -83,6 +83,10 @@ void or_qk_norm_rope(int dtype, void* q, void* k,
                      const int32_t* positions, int64_t rows,
                      float theta, float eps);
 
+void or_apply_rope_interleaved(float* q, float* k, int n_q_heads, int n_kv_heads,
+                               int q_head_stride, int k_head_stride, int rot_dim, int pos,
+                               float theta);
+
 void or_qk_norm_rope_kv(int dtype, void* q, void* k, const void* v, int64_t q_row_stride,
                         int64_t k_row_stride, int64_t v_row_stride, int q_head_stride,
                         int k_head_stride, int v_head_stride, int n_q_heads, int n_kv_heads,

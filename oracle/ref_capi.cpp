@@ -89,6 +89,27 @@ int ref_sample_token(const float* logits, int vocab, float temperature, float re
     return tok;
 }
 
+/* The decode loop's use of sample_token (generate.cpp:80, :129; the
+ * generated tokens are the history, :87):
+ * srand48(seed) once, then `steps` calls, each appending the token it
+ * returns to the history; step i reads logits row i % nrows. */
+void ref_sample_token_loop(const float* logits, int nrows, int vocab, float temperature,
+                           float rep, int ctx, float freq, const int32_t* hist0, int hist0_len,
+                           long seed, int steps, int32_t* tokens_out) {
+    ane_lm::SamplingParams p;
+    p.temperature = temperature;
+    p.repetition_penalty = rep;
+    p.repetition_context_size = ctx;
+    p.frequency_penalty = freq;
+    std::vector<int> recent(hist0, hist0 + (hist0_len > 0 ? hist0_len : 0));
+    srand48(seed);
+    for (int i = 0; i < steps; i++) {
+        int tok = ane_lm::sample_token(logits + (size_t)(i % nrows) * vocab, vocab, p, recent);
+        tokens_out[i] = tok;
+        recent.push_back(tok);
+    }
+}
+
 /* rmsnorm_gated (core/cpu_ops.cpp:33-39) and l2_normalize (:106-111). */
 void ref_rmsnorm_gated(float* out, const float* x, const float* z, const float* w, int dim) {
     ane_lm::rmsnorm_gated(out, x, z, w, dim);

@@ -64,6 +64,8 @@ def load_oracle() -> C.CDLL:
     lib.or_decode_attention.argtypes = [C.c_int, _p, _i64, _p, _i64, C.c_int, _p, _p, _i64,
                                         _p, _p, C.c_int, _i64, C.c_int, C.c_int, C.c_int]
     lib.or_kv_ring_advance.restype = C.c_int
+    lib.or_apply_rope_interleaved.argtypes = [_p, _p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              C.c_int, _f]
     lib.or_qk_norm_rope_kv.argtypes = [C.c_int, _p, _p, _p, _i64, _i64, _i64, C.c_int, C.c_int,
                                        C.c_int, C.c_int, C.c_int, C.c_int, _p, _p, _p, _p, _p,
                                        _i64, _p, _i64, _f, _f]
@@ -101,6 +103,8 @@ def load_ref():
     lib.ref_sample_token.restype = C.c_int
     lib.ref_sample_token.argtypes = [_p, C.c_int, _f, _f, C.c_int, _f, _p, C.c_int, C.c_long,
                                      C.POINTER(_f)]
+    lib.ref_sample_token_loop.argtypes = [_p, C.c_int, C.c_int, _f, _f, C.c_int, _f, _p, C.c_int,
+                                          C.c_long, C.c_int, _p]
     lib.ref_write_ane_blobs.restype = C.c_int
     lib.ref_write_ane_blobs.argtypes = [C.c_char_p, C.c_char_p]
     lib.ref_layer_chain_f16.argtypes = [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64,
@@ -219,6 +223,14 @@ class Oracle:
                                      _ptr(np.ascontiguousarray(length, np.int32)), cap, B, H, hk,
                                      hd)
         return out
+
+    def apply_rope_interleaved(self, q, k, rot_dim, pos, theta):
+        """apply_rope_cached without tables (the reference's fallback) on
+        fp32 q [n_q, hd] and k [n_kv, hd]; returns new arrays."""
+        q, k = np.array(q, np.float32, copy=True), np.array(k, np.float32, copy=True)
+        self.lib.or_apply_rope_interleaved(_ptr(q), _ptr(k), q.shape[0], k.shape[0], q.shape[1],
+                                           k.shape[1], rot_dim, pos, theta)
+        return q, k
 
     def qk_norm_rope_kv(self, qkv, nq, nkv, hd, qw, kw, pos, theta, k_cache, v_cache, slots,
                         per_row_cache=False, eps=1e-6):

@@ -140,14 +140,14 @@ def test_decode_attention_unsupported_shapes(ane, head_dim, heads, kv):
 
 
 def test_workspace_size_rule(ane):
-    """No workspace with one split (max_len <= 64); counters + (m, l) + o per
-    split otherwise, each 256-byte aligned."""
+    """No workspace with one split (max_len <= 64); (m, l) + o per split
+    otherwise, each 256-byte aligned."""
     L = ane.lib()
     assert L.ane_cuda_decode_attention_workspace_size(4, 16, 8, 128, 64) == 0
     n = L.ane_cuda_decode_attention_workspace_size(4, 16, 8, 128, 4096)
     splits = 4096 // 64
     r = lambda v: (v + 255) // 256 * 256  # noqa: E731
-    assert n == r(4 * 8 * 4) + r(4 * 16 * splits * 2 * 4) + r(4 * 16 * splits * 128 * 4)
+    assert n == r(4 * 16 * splits * 2 * 4) + r(4 * 16 * splits * 128 * 4)
     assert L.ane_cuda_decode_attention_workspace_size(-1, 16, 8, 128, 64) == -1
     assert L.ane_cuda_decode_attention_static_capacity() == 16 << 20
 

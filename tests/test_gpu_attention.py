@@ -154,8 +154,9 @@ def test_attention_matches_reference(ane, ref, shape):
 
 
 def test_attention_caller_workspace_two_calls(ane, oracle):
-    """A caller-provided zero-filled workspace gives the same bits as the
-    library-held one, twice in a row (the split counters are left at zero)."""
+    """A caller workspace full of garbage (it needs no clearing: only the
+    call in flight keeps its split partials there) gives the same bits as
+    the library-held one, twice in a row."""
     torch = _torch()
     rng = np.random.default_rng(11)
     B, H, hk, hd, cap = 2, 16, 8, 128, 1024
@@ -163,20 +164,19 @@ def test_attention_caller_workspace_two_calls(ane, oracle):
     want = oracle.decode_attention(q, k, v, st, ln)
     nbytes = ane.decode_attention_workspace_size(B, H, hk, hd, cap)
     assert nbytes > 0
-    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ws = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device="cuda")
     for _ in range(2):
         got = run_gpu(ane, q, k, v, st, ln, "f32", workspace=ws)
         assert np.array_equal(bits(got), bits(want))
-    assert int(ws[: B * hk * 4].count_nonzero()) == 0
     got = run_gpu(ane, q, k, v, st, ln, "f32")
     assert np.array_equal(bits(got), bits(want))
 
 
 def test_attention_workspace_reused_across_shapes(ane, oracle):
     """One workspace (the caller's, then the library's own) serving calls of
-    different shapes in turn: a small batch writes split partials where the
-    next, larger batch keeps its split counters.  Every call must still give
-    the oracle's bits."""
+    different shapes in turn: each call's partials land where the previous
+    call of another shape kept its own.  Every call must still give the
+    oracle's bits."""
     torch = _torch()
     rng = np.random.default_rng(77)
     cases = [(1, 16, 8, 128, 4096, [9], [4096]),
@@ -191,6 +191,91 @@ def test_attention_workspace_reused_across_shapes(ane, oracle):
             want = oracle.decode_attention(q, k, v, st, ln)
             got = run_gpu(ane, q, k, v, st, ln, "f32", workspace=workspace)
             assert np.array_equal(bits(got), bits(want)), (B, H, cap, workspace is None)
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_attention_graph_replay_between_other_shapes(ane, oracle, dt):
+    """A call captured in a CUDA graph, replayed after eager calls of other
+    shapes on the same workspace (whose partials cover the captured call's
+    part of it) and after a replay of another graph: every replay gives the
+    same bits as the eager call."""
+    torch = _torch()
+    rng = np.random.default_rng(31)
+    X = (1, 16, 8, 128, 4096, [1000], [4096])
+    Y = (16, 32, 8, 128, 1024, list(rng.integers(0, 1024, 16)), list(rng.integers(1, 1025, 16)))
+    size = max(ane.decode_attention_workspace_size(B, H, hk, hd, cap) for B, H, hk, hd, cap, _, _ in (X, Y))
+    ws = torch.full((size,), 0x7F, dtype=torch.uint8, device="cuda")
+
+    def dev_case(c):
+        B, H, hk, hd, cap, starts, lens = c
+        host = make_case(rng, B, H, hk, hd, cap, starts, lens, dt)
+        d = [to_dev(a, dt) for a in host[:3]] + [torch.from_numpy(a).cuda() for a in host[3:]]
+        return host, d, torch.empty_like(d[0])
+
+    (hx, dx, ox), (hy, dy, oy) = dev_case(X), dev_case(Y)
+    want_x = oracle.decode_attention(*hx)
+    vmax = float(np.abs(as_f32(hx[2], dt)).max())
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        ane.decode_attention(*dx, out=ox, workspace=ws)  # eager warm-up of X
+        s.synchronize()
+        eager_x = to_host(ox.clone(), dt)
+        gx, gy = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gx, stream=s):
+            ane.decode_attention(*dx, out=ox, workspace=ws)
+        with torch.cuda.graph(gy, stream=s):
+            ane.decode_attention(*dy, out=oy, workspace=ws)
+        for order in ("eager_y", "replay_y", "both"):
+            ox.zero_()
+            if order in ("eager_y", "both"):
+                ane.decode_attention(*dy, out=oy, workspace=ws)
+            if order in ("replay_y", "both"):
+                gy.replay()
+            gx.replay()
+            s.synchronize()
+            got = to_host(ox, dt)
+            assert np.array_equal(bits(got), bits(eager_x)), order
+        del gx, gy
+    check_against_oracle(eager_x, want_x, dt, vmax)
+
+
+def test_attention_held_workspace_not_grown_during_capture(ane, oracle):
+    """The library-held workspace of a stream is never allocated during a
+    stream capture: such a call is refused with a clear error (the capture
+    itself stays valid), and after one eager call of the shape the same
+    capture works and replays to the oracle's bits."""
+    torch = _torch()
+    rng = np.random.default_rng(41)
+    host = make_case(rng, 1, 16, 8, 128, 4096, [5], [4096], "f32")
+    want = oracle.decode_attention(*host)
+    d = [to_dev(a, "f32") for a in host[:3]] + [torch.from_numpy(a).cuda() for a in host[3:]]
+    out = torch.empty_like(d[0])
+    # max_len far above the keys sizes a workspace (about 136 MB) larger
+    # than any earlier call gave a pooled stream, so this call must grow it
+    big = 1 << 20
+    assert ane.decode_attention_workspace_size(1, 16, 8, 128, big) > 100 << 20
+    s = torch.cuda.Stream()
+    err = None
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            try:
+                ane.decode_attention(*d, out=out, max_len=big)
+            except ane.AneCudaError as e:
+                err = e
+        assert err is not None and err.status == ane.ERR_INVALID_ARG
+        assert "capture" in str(err)
+        del g
+        ane.decode_attention(*d, out=out, max_len=big)  # eager: grows the stream's workspace
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            ane.decode_attention(*d, out=out, max_len=big)
+        out.zero_()
+        g.replay()
+        s.synchronize()
+        assert np.array_equal(bits(to_host(out, "f32")), bits(want))
+        del g
 
 
 def test_attention_max_len_sizes_launch(ane, oracle):

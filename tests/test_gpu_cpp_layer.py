@@ -1,6 +1,7 @@
 """GPU: the reference-signature C++ layer (ane-lm_b200/core/cuda_ops.h), driven
 by a C++ program compiled here against the library, checked against the
 oracle -- the path a maintainer takes when dropping it into ANE-LM."""
+import ctypes as C
 import os
 import subprocess
 
@@ -76,11 +77,12 @@ def test_reference_signature_layer(checker, oracle):
     a0, a1 = heads[:, :hd // 2], heads[:, hd // 2:]
     want = np.concatenate([a0 * cosr - a1 * sinr, a1 * cosr + a0 * sinr], 1).ravel()
     assert np.array_equal(take(np.float32, qk.size), want)
-    # no tables: cos/sin of the pinned sincos at the position, in registers
-    inv = oracle.rope_inv_freq(hd, 1e6)
-    sc = np.array([oracle.sincosf(np.float32(777) * f) for f in inv], np.float32)
-    s_, c_ = sc[:, 0], sc[:, 1]
-    want = np.concatenate([a0 * c_ - a1 * s_, a1 * c_ + a0 * s_], 1).ravel()
+    # no tables: the reference's fallback over interleaved pairs
+    # (core/cpu_ops.cpp:66-77), cos/sin of the pinned sincos in registers
+    nh = heads.shape[0]
+    wq, wk = oracle.apply_rope_interleaved(heads[:nq], heads[nq:], hd, 777, 1e6)
+    want = np.concatenate([wq, wk]).ravel()
+    assert nh == nq + nkv
     assert np.array_equal(take(np.float32, qk.size), want)
     # silu_vec_inplace / mul_sigmoid_inplace (fp32: pinned exp, IEEE divide)
     assert np.array_equal(take(np.float32, n), oracle.silu_mul(g[None], np.ones((1, n), np.float32))[0])
@@ -119,3 +121,42 @@ def test_reference_signature_layer(checker, oracle):
     # a failing call reports through last_status() and the process carries on
     assert take(np.int32, 1)[0] == 1
     assert off == len(raw)
+
+
+def test_sample_token_decode_loop(ane, ref, tmp_path):
+    """1,000 decode steps through the drop-in sample_token with a growing
+    history (Qwen3 vocabulary, T 0.6, penalty 1.2 over the last 256 ids,
+    frequency 0.1): every token equals the reference's own loop with the
+    same srand48 seed, and the device's free memory does not change after
+    the first call (the staging is fixed: only the window is copied)."""
+    exe = str(tmp_path / "sample_loop")
+    subprocess.run(["g++", "-O2", "-std=c++17", os.path.join(TESTS, "cpp", "sample_loop.cpp"),
+                    "-I", os.path.join(REPO, "include"), "-I", os.path.join(PKG, "core"),
+                    "-I", f"{CUDA}/include", "-L", PKG, "-lane_cuda", "-L", f"{CUDA}/lib64",
+                    "-lcudart", f"-Wl,-rpath,{PKG}", f"-Wl,-rpath,{CUDA}/lib64", "-o", exe],
+                   check=True)
+    rng = np.random.default_rng(99)
+    nrows, vocab, ctx, steps, seed = 8, 151936, 256, 1000, 4321
+    logits = (rng.standard_normal((nrows, vocab)) * 3).astype(np.float32)
+    # a peaked row or two, so the history repeats ids and the penalties bite
+    logits[3, 5:9] += 30.0
+    hist0 = rng.integers(0, vocab, 100).astype(np.int32)
+    temp, rep, freq = 0.6, 1.2, 0.1
+    inp, outp = tmp_path / "in.bin", tmp_path / "out.bin"
+    with open(inp, "wb") as f:
+        f.write(np.array([nrows, vocab, ctx, hist0.size, steps, seed], np.int32).tobytes())
+        f.write(np.array([temp, rep, freq], np.float32).tobytes())
+        f.write(logits.tobytes())
+        f.write(hist0.tobytes())
+    subprocess.run([exe, str(inp), str(outp)], check=True, timeout=300)
+    raw = outp.read_bytes()
+    got = np.frombuffer(raw, np.int32, steps)
+    mem = np.frombuffer(raw, np.int64, 2, steps * 4)
+    want = np.empty(steps, np.int32)
+    ref.ref_sample_token_loop(logits.ctypes.data_as(C.c_void_p), nrows, vocab, np.float32(temp),
+                              np.float32(rep), ctx, np.float32(freq),
+                              hist0.ctypes.data_as(C.c_void_p), hist0.size, seed, steps,
+                              want.ctypes.data_as(C.c_void_p))
+    assert np.array_equal(got, want), int(np.argmax(got != want))
+    assert len(set(want.tolist())) < steps  # repeats: the penalties were exercised
+    assert mem[0] == mem[1], mem

@@ -77,6 +77,27 @@ def test_rope_inv_freq_matches_model_table(oracle, ref):
         assert abs(c - cos[j]) <= 2 ** -23 and abs(s - sin[j]) <= 2 ** -23
 
 
+def test_rope_fallback_matches_reference(oracle, ref):
+    """apply_rope_cached without tables takes the reference's fallback over
+    interleaved pairs with libm powf / cosf / sinf (core/cpu_ops.cpp:66-77);
+    the restatement (pinned inv_freq and sincos) stays within 1e-6 x max|v|
+    of the reference build, at positions 0 .. 2^20 and two rotary widths."""
+    import ctypes as C
+    rng = np.random.default_rng(21)
+    for pos in (0, 1, 2, 7, 100, 777, 2047, 4095, 16383, 100000, 1 << 20):
+        for rot in (128, 64):
+            q = rng.standard_normal((16, 128)).astype(np.float32)
+            k = rng.standard_normal((8, 128)).astype(np.float32)
+            oq, ok = oracle.apply_rope_interleaved(q, k, rot, pos, 1e6)
+            rq, rk = q.copy(), k.copy()
+            ref.ref_apply_rope_cached(ptr(rq), ptr(rk), 16, 8, 128, 128, 128, rot, pos,
+                                      np.float32(1e6), None, None)
+            vmax = max(np.abs(q).max(), np.abs(k).max())
+            assert np.abs(oq - rq).max() <= 1e-6 * vmax and np.abs(ok - rk).max() <= 1e-6 * vmax
+            # elements past rot_dim are untouched
+            assert np.array_equal(oq[:, rot:], q[:, rot:]) and np.array_equal(rq[:, rot:], q[:, rot:])
+
+
 # ---------------------------------------------------------------- rmsnorm
 def test_rmsnorm_f32_golden(oracle):
     g = gold("rmsnorm.npz")

@@ -27,7 +27,7 @@ def test_static_matches_regular_two_calls(ane, dt_name):
     q, k, v, st, ln = _case(torch, 2, 32, 8, 128, 2048, [100, 0], [2048, 777], dt, 5)
     want = ane.decode_attention(q, k, v, st, ln).float()
     vmax = v.float().abs().max().item()
-    for _ in range(2):  # the second call starts from the counters the first left
+    for _ in range(2):  # the second call finds the first call's partials in the array
         got = ane.decode_attention_static(q, k, v, st, ln).float()
         torch.cuda.synchronize()
         assert (got - want).abs().max().item() <= TOL * vmax
