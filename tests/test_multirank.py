@@ -150,3 +150,11 @@ def test_two_gloo_ranks_shard_rows_without_a_data_path_collective():
     # the reference arm printed nothing on rank 1 and returned at once
     quiet, dt = got[1][9]
     assert quiet and dt < 1.0
+
+
+def test_per_kernel_events_on_a_subset_of_steps():
+    import bench
+    for steps in (1, 2, 3, 4, 20, 200):
+        marked = [i for i in range(steps) if bench.instrumented(i, steps)]
+        assert marked and len(marked) <= max(1, steps // bench.EVENT_EVERY)
+        assert all(0 <= i < steps for i in marked)
