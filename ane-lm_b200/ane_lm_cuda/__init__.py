@@ -36,6 +36,8 @@ _SIGS = {
     "ane_cuda_read_status_flags": (_i, [C.POINTER(C.c_uint32), _i]),
     "ane_cuda_bf16_to_f16": (_i, [_p, _p, _i64, _p]),
     "ane_cuda_embedding_gather": (_i, [_p, _i, _p, _i, _p, _i64, _i, _i, _p]),
+    "ane_cuda_embedding_rmsnorm": (_i, [_i, _p, _i64, _p, _i64, _p, _i, _p, _i64, _i, _i, _i, _p,
+                                        _f, _p]),
     "ane_cuda_residual_rmsnorm": (_i, [_i, _p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _f, _p]),
     "ane_cuda_qk_norm_rope": (_i, [_i, _p, _p, _i64, _i64, _i, _i, _i, _i, _i, _i, _p, _p, _p,
                                    _i64, _f, _f, _p]),
@@ -158,6 +160,25 @@ def embedding_gather(table, ids, out_dtype=None, out=None):
         _ptr(out), _dt(out), _ptr(table), _dt(table), _ptr(ids), ids.numel(), vocab, hidden,
         _stream(table)))
     return out
+
+
+def embedding_rmsnorm(table, ids, weight, x=None, accumulate=False, out_dtype=None, out=None,
+                      eps=1e-6):
+    """x = table[ids] widened to out_dtype (or x += table[ids] with accumulate);
+    returns rmsnorm(x) * weight.  x is written in place when given."""
+    torch = _torch()
+    _cuda(table, ids, weight, x, out)
+    vocab, hidden = table.shape
+    odt = (table.dtype if out_dtype is None else out_dtype) if x is None else x.dtype
+    ids = ids.to(torch.int32).contiguous()
+    if x is None:
+        x = torch.empty((ids.numel(), hidden), dtype=odt, device=table.device)
+    if out is None:
+        out = torch.empty_like(x)
+    _check("embedding_rmsnorm", lib().ane_cuda_embedding_rmsnorm(
+        _dt(x), _ptr(x), x.stride(0), _ptr(out), out.stride(0), _ptr(table), _dt(table), _ptr(ids),
+        ids.numel(), vocab, hidden, int(accumulate), _ptr(weight), eps, _stream(table)))
+    return x, out
 
 
 def residual_rmsnorm(x, d, weight, out=None, eps=1e-6):

@@ -231,6 +231,14 @@ void embedding_gather(void* out, ane_cuda_dtype out_dtype, const void* table,
                                                        rows, vocab, hidden, t_stream));
 }
 
+void embedding_rmsnorm(void* x, void* out, ane_cuda_dtype out_dtype, const void* table,
+                       ane_cuda_dtype table_dtype, const int32_t* ids, int64_t rows, int vocab,
+                       int hidden, bool accumulate, const float* weight, float eps) {
+    note("embedding_rmsnorm",
+         ane_cuda_embedding_rmsnorm(out_dtype, x, hidden, out, hidden, table, table_dtype, ids, rows,
+                                    vocab, hidden, accumulate ? 1 : 0, weight, eps, t_stream));
+}
+
 void sample_rows(const float* logits, int64_t rows, int vocab, const int32_t* history,
                  const int32_t* history_len, int64_t history_stride, const float* uniforms,
                  const SamplingParams& p, int32_t* out_tokens) {

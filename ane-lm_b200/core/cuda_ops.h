@@ -90,6 +90,11 @@ void silu_mul(ane_cuda_dtype dtype, void* out, const void* gate, const void* up,
 void embedding_gather(void* out, ane_cuda_dtype out_dtype, const void* table,
                       ane_cuda_dtype table_dtype, const int32_t* ids, int64_t rows, int vocab,
                       int hidden);
+// x = table[ids] (accumulate: x += table[ids]), out = rmsnorm(x) * weight, in
+// one launch (models/llm/qwen3.cpp:498 then :503); ane_cuda_embedding_rmsnorm.
+void embedding_rmsnorm(void* x, void* out, ane_cuda_dtype out_dtype, const void* table,
+                       ane_cuda_dtype table_dtype, const int32_t* ids, int64_t rows, int vocab,
+                       int hidden, bool accumulate, const float* weight, float eps = 1e-6f);
 void sample_rows(const float* logits, int64_t rows, int vocab, const int32_t* history,
                  const int32_t* history_len, int64_t history_stride, const float* uniforms,
                  const SamplingParams& params, int32_t* out_tokens);

@@ -405,6 +405,7 @@ int ane_cuda_qk_norm_rope(int dtype, void* q, void* k, int64_t q_row_stride,
     if (!valid_dtype(dtype)) return fail(ANE_CUDA_ERR_INVALID_ARG, "qk_norm_rope: bad dtype %d", dtype);
     QkArgs a{q, k, q_row_stride, k_row_stride, q_head_stride, k_head_stride, n_q_heads, n_kv_heads,
              head_dim, rot_dim, q_weight, k_weight, positions, 0, rows, eps, nullptr, nullptr};
+    a.flags = status_flags_device();
     int st = validate("qk_norm_rope", a);
     if (st) return st;
     if (rows == 0) return ANE_CUDA_OK;

@@ -113,6 +113,23 @@ ANE_CUDA_API int ane_cuda_residual_rmsnorm(int dtype, void* x, int64_t x_stride,
                               const float* weight, int64_t rows, int dim, float eps,
                               void* stream);
 
+/* The decode step's first two ops in one launch: the embedding gather
+ * (models/llm/qwen3.cpp:498) and the RMSNorm that reads it (:503; with
+ * accumulate, the residual add before it, :516-518).  Per row r: e =
+ * table[ids[r]] widened to out_dtype (exact), x[r] = e (accumulate = 0) or
+ * x[r] + e (accumulate = 1), stored; out[r] = (x[r] * inv) * weight as in
+ * ane_cuda_residual_rmsnorm.  The same bits as ane_cuda_embedding_gather
+ * followed by ane_cuda_residual_rmsnorm.  out_dtype equals table_dtype, or
+ * is F32 with an F16 / BF16 table; hidden a multiple of 16 bytes of
+ * out_dtype, at most 4096 fp16 / 2048 fp32 elements; x, out and weight
+ * 16-byte aligned.  An id outside [0, vocab) reads as a zero row and sets
+ * ANE_CUDA_FLAG_BAD_TOKEN_ID. */
+ANE_CUDA_API int ane_cuda_embedding_rmsnorm(int out_dtype, void* x, int64_t x_stride, void* out,
+                                            int64_t out_stride, const void* table, int table_dtype,
+                                            const int32_t* ids, int64_t rows, int vocab, int hidden,
+                                            int accumulate, const float* weight, float eps,
+                                            void* stream);
+
 /* ---- per-head QK-norm + RoPE ------------------------------------------
  * Replaces the per-head rmsnorm of q and k (models/llm/qwen3.cpp:444-461)
  * followed by apply_rope_cached (core/cpu_ops.cpp:56-80, half-split fast

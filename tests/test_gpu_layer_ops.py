@@ -79,6 +79,77 @@ def test_residual_rmsnorm(ane, oracle, dt, dim, with_d):
     check(to_host(y, dt), yo, dt, "rmsnorm")
 
 
+# Many rows (several waves of CTAs, ragged counts that leave the last wave
+# partial): the same bits as the oracle, row by row.
+@pytest.mark.parametrize("dt,dim", [("f16", 4096), ("f16", 1024), ("bf16", 4096), ("bf16", 2048),
+                                    ("f32", 2048), ("f32", 1024)])
+@pytest.mark.parametrize("rows", [512, 1001, 5003])
+@pytest.mark.parametrize("with_d", [True, False])
+def test_residual_rmsnorm_many_rows(ane, oracle, dt, dim, rows, with_d):
+    rng = np.random.default_rng(rows + dim + 7 * with_d)
+    x = rand(rng, (rows, dim), dt, outliers=0.001)
+    d = rand(rng, (rows, dim), dt) if with_d else None
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    xt, dt_ = to_dev(x, dt), (to_dev(d, dt) if with_d else None)
+    y = ane.residual_rmsnorm(xt, dt_, to_dev(w, "f32"))
+    xo, yo = oracle.residual_rmsnorm(x, d, w)
+    assert np.array_equal(to_host(xt, dt), xo)
+    got = to_host(y, dt)
+    check(got, yo, dt, "rmsnorm many rows")
+    assert np.array_equal(got.view(np.uint8), yo.view(np.uint8))  # same orders: same bits
+
+
+def test_residual_rmsnorm_many_rows_strided(ane, oracle):
+    """Row strides above the width (16-byte multiples) over many rows."""
+    rng = np.random.default_rng(44)
+    rows, dim, pitch = 777, 2048, 2048 + 64
+    xb = rand(rng, (rows, pitch), "f16")
+    db = rand(rng, (rows, pitch), "f16")
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    xt, dt_ = to_dev(xb, "f16"), to_dev(db, "f16")
+    out = to_dev(np.zeros((rows, pitch), np.float16), "f16")
+    ane.residual_rmsnorm(xt[:, :dim], dt_[:, :dim], to_dev(w, "f32"), out=out[:, :dim])
+    xo, yo = oracle.residual_rmsnorm(xb[:, :dim].copy(), db[:, :dim].copy(), w)
+    gx, gy = to_host(xt, "f16"), to_host(out, "f16")
+    assert np.array_equal(gx[:, :dim], xo) and np.array_equal(gx[:, dim:], xb[:, dim:])
+    assert np.array_equal(gy[:, :dim], yo) and not gy[:, dim:].any()
+
+
+# The decode step's gather + (residual) RMSNorm in one launch: the same bits
+# as the gather followed by the norm; bad ids read as zero rows and flag.
+@pytest.mark.parametrize("tdt,odt", [("f16", "f32"), ("bf16", "f32"), ("f16", "f16"),
+                                     ("bf16", "bf16"), ("f32", "f32")])
+@pytest.mark.parametrize("hidden", [1024, 2048])
+@pytest.mark.parametrize("acc", [False, True])
+@pytest.mark.parametrize("rows", [1, 37])
+def test_embedding_rmsnorm(ane, oracle, tdt, odt, hidden, acc, rows):
+    torch = _torch()
+    rng = np.random.default_rng(hidden + rows + 3 * acc)
+    vocab = 1000
+    table = rand(rng, (vocab, hidden), tdt, scale=0.5)
+    ids = rng.integers(0, vocab, rows).astype(np.int32)
+    if rows > 2:
+        ids[1], ids[2] = -1, vocab  # outside the vocabulary
+    w = (1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    x0 = rand(rng, (rows, hidden), odt) if acc else None
+    ane.read_status_flags(clear=True)
+    xt = to_dev(x0, odt) if acc else None
+    odt_t = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[odt]
+    x, y = ane.embedding_rmsnorm(to_dev(table, tdt), torch.from_numpy(ids).cuda(), to_dev(w, "f32"),
+                                 x=xt, accumulate=acc, out_dtype=odt_t)
+    flags = ane.read_status_flags(clear=True)
+    assert bool(flags & ane.FLAG_BAD_TOKEN_ID) == (rows > 2)
+    code = {"f32": 0, "f16": 1, "bf16": 2}[odt]
+    e, bad = oracle.embedding_gather(table, ids, out_dtype=code)
+    assert bad == (2 if rows > 2 else 0)
+    xo, yo = oracle.residual_rmsnorm(x0, e, w) if acc else oracle.residual_rmsnorm(e, None, w)
+    if not acc:
+        xo = e
+    gx, gy = to_host(x, odt), to_host(y, odt)
+    assert np.array_equal(gx.view(np.uint8), np.ascontiguousarray(xo).view(np.uint8))
+    assert np.array_equal(gy.view(np.uint8), np.ascontiguousarray(yo).view(np.uint8))
+
+
 def test_rmsnorm_in_place_and_strided(ane, oracle):
     torch = _torch()
     rng = np.random.default_rng(3)
@@ -124,6 +195,28 @@ def test_qk_norm_rope(ane, oracle, dt, case):
     check(got, want, dt, f"qk {case}")
     v0 = (nq + nkv) * hd
     assert np.array_equal(got[:, v0:].view(np.uint8), qkv[:, v0:].view(np.uint8))  # v untouched
+
+
+# Many rows of the fused layout (several waves, ragged counts).
+@pytest.mark.parametrize("dt", ["f16", "f32", "bf16"])
+@pytest.mark.parametrize("case", [(32, 8, 128, 128), (16, 8, 128, 128), (8, 2, 64, 64)])
+@pytest.mark.parametrize("rows", [512, 3001])
+def test_qk_norm_rope_many_rows(ane, oracle, dt, case, rows):
+    torch = _torch()
+    nq, nkv, hd, rot = case
+    rng = np.random.default_rng(nq * 7 + rows)
+    qkv = rand(rng, (rows, (nq + 2 * nkv) * hd), dt, outliers=0.001)
+    qw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    kw = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    pos = rng.integers(0, 40000, rows).astype(np.int32)
+    pos[:4] = [0, 1, 4095, 1 << 20]
+    t = to_dev(qkv, dt)
+    ane.qk_norm_rope(t, to_dev(qw, "f32"), to_dev(kw, "f32"), torch.from_numpy(pos).cuda(), nq,
+                     nkv, hd, theta=1e6, rot_dim=rot)
+    want = oracle.qk_norm_rope(qkv, nq, nkv, hd, qw, kw, pos, 1e6, rot_dim=rot)
+    got = to_host(t, dt)
+    check(got, want, dt, f"qk many rows {case}")
+    assert np.array_equal(got.view(np.uint8), want.view(np.uint8))  # same orders: same bits
 
 
 def test_rope_only_without_norm(ane, oracle):
