@@ -321,9 +321,13 @@ sample_rows_kernel(const SampArgs a) {
     // ---- pass 1: max, four groups in flight per thread ----
     // fmaxf skips NaN like the reference's `>` scan (vDSP_maxv); NaNs are
     // counted on the side.
+    // (back to front: the exp-sum pass then starts on the lines read last,
+    // which are still in L2)
     float mx = -INFINITY;
     bool nan_seen = false;
-    for (int g0 = 0; g0 < ngroups; g0 += 4 * kSampThreads) {
+    const int nsweep = (ngroups + 4 * kSampThreads - 1) / (4 * kSampThreads);
+    for (int sw = nsweep - 1; sw >= 0; sw--) {
+        const int g0 = sw * 4 * kSampThreads;
         float v[4][4];
 #pragma unroll
         for (int u = 0; u < 4; u++) {
@@ -355,35 +359,33 @@ sample_rows_kernel(const SampArgs a) {
     }
 
     // ---- pass 2: pinned sum of exp over the 1024 virtual threads ----
+    // Two steps of 1024 groups per iteration, all four loads issued first
+    // (64 bytes in flight per thread), then the exps and the adds in order.
     float acc_lo = 0.0f, acc_hi = 0.0f;
-    for (int g0 = 0; g0 < ngroups; g0 += kVirtThreads) {
-        const int ga = g0 + tid, gb = g0 + tid + kSampThreads;
-        float va[4], vb[4];
+    auto add4 = [&](const float (&v)[4], int g, float& acc) {
+        float d[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) d[j] = __fadd_rn(__fmul_rn(v[j], inv_t), neg_m);
+        const float2 e01 = pinned_expf_nonpos2(make_float2(d[0], d[1]));
+        const float2 e23 = pinned_expf_nonpos2(make_float2(d[2], d[3]));
+        const float e[4] = {e01.x, e01.y, e23.x, e23.y};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (g * 4 + j < a.vocab) acc = __fadd_rn(acc, e[j]);
+    };
+    for (int g0 = 0; g0 < ngroups; g0 += 2 * kVirtThreads) {
+        const int ga = g0 + tid, gb = ga + kSampThreads;
+        const int gc = ga + kVirtThreads, gd = gb + kVirtThreads;
+        float va[4], vb[4], vc[4], vd[4];
         if (ga < ngroups) load4(a, lrow, P, ga * 4, va);
         if (gb < ngroups) load4(a, lrow, P, gb * 4, vb);
-        // the exps two at a time (packed), the adds in order
-        if (ga < ngroups) {
-            float d[4], e[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) d[j] = __fadd_rn(__fmul_rn(va[j], inv_t), neg_m);
-            const float2 e01 = pinned_expf_nonpos2(make_float2(d[0], d[1]));
-            const float2 e23 = pinned_expf_nonpos2(make_float2(d[2], d[3]));
-            e[0] = e01.x; e[1] = e01.y; e[2] = e23.x; e[3] = e23.y;
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (ga * 4 + j < a.vocab) acc_lo = __fadd_rn(acc_lo, e[j]);
-        }
-        if (gb < ngroups) {
-            float d[4], e[4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) d[j] = __fadd_rn(__fmul_rn(vb[j], inv_t), neg_m);
-            const float2 e01 = pinned_expf_nonpos2(make_float2(d[0], d[1]));
-            const float2 e23 = pinned_expf_nonpos2(make_float2(d[2], d[3]));
-            e[0] = e01.x; e[1] = e01.y; e[2] = e23.x; e[3] = e23.y;
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (gb * 4 + j < a.vocab) acc_hi = __fadd_rn(acc_hi, e[j]);
-        }
+        if (gc < ngroups) load4(a, lrow, P, gc * 4, vc);
+        if (gd < ngroups) load4(a, lrow, P, gd * 4, vd);
+        // virtual thread t: groups ga then gc; t + 512: gb then gd
+        if (ga < ngroups) add4(va, ga, acc_lo);
+        if (gb < ngroups) add4(vb, gb, acc_hi);
+        if (gc < ngroups) add4(vc, gc, acc_lo);
+        if (gd < ngroups) add4(vd, gd, acc_hi);
     }
     const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
 
@@ -398,14 +400,13 @@ sample_rows_kernel(const SampArgs a) {
         S.start = 0;
         S.result = -1;
     }
-    // ---- pass 3a: the first tile by one warp --------------------------------
-    // While cum is small it crosses a binade every few elements, and each
+    // ---- pass 3a: the first tile, serially -----------------------------------
+    // While cum is small it leaves its binade every few elements, and each
     // crossing would cost a block-wide round.  So the CTA computes every p of
-    // the first tile into shared memory, and warp 0 scans it in windows of
-    // 256 elements (8 per lane) with warp-wide scans only: the same unit
-    // arithmetic, events and serial fp32 adds as the block rounds below.  The
-    // first window without an event ends it: events have become sparse, and
-    // the block rounds take the rest of the tile faster.
+    // the first tile into shared memory and one thread adds them in fp32 --
+    // the reference's own loop, eight elements per branch -- until a stretch
+    // of 256 elements passes without a change of binade; from there the
+    // block rounds below take over with the unit arithmetic.
     {
         const int t0end = min(kTile, a.vocab);
         float* const pt = &cbuf[0][0];  // kTile floats
@@ -422,71 +423,38 @@ sample_rows_kernel(const SampArgs a) {
             }
         }
         __syncthreads();
-        if (w == 0) {
-            while (true) {
-                const int start = S.start;
-                if (start >= t0end || S.result >= 0) break;  // warp-uniform
-                const uint32_t ucum = S.ucum, tr = S.tr;
-                const int E = S.E;
-                uint32_t k[kPerThread];
-                bool ser[kPerThread];
-                uint32_t kt = 0;
+        if (tid == 0) {
+            float cum = 0.0f;
+            int j = 0, hit = -1;
+            while (j < t0end) {
+                const int jend = min(t0end, j + kWarp * kPerThread);
+                const uint32_t e0 = __float_as_uint(cum) >> 23;
+                for (; j + 8 <= jend; j += 8) {
+                    float pv[8], cs[8];
 #pragma unroll
-                for (int q = 0; q < kPerThread; q++) {
-                    const int i = start + lane * kPerThread + q;
-                    bool tie = false, big = false;
-                    k[q] = 0;
-                    if (i < t0end) classify(pt[i], E, k[q], tie, big);
-                    ser[q] = tie || big;
-                    kt = sat_add(kt, ser[q] ? kSat : k[q]);
-                }
-                uint32_t inc = kt;
+                    for (int q = 0; q < 8; q++) pv[q] = pt[j + q];
+                    cs[0] = __fadd_rn(cum, pv[0]);
 #pragma unroll
-                for (int off = 1; off < 32; off <<= 1) {
-                    const uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
-                    if (lane >= off) inc = sat_add(inc, o);
-                }
-                const uint32_t all = __shfl_sync(0xffffffffu, inc, 31);
-                uint32_t excl = __shfl_up_sync(0xffffffffu, inc, 1);
-                if (lane == 0) excl = 0;
-                uint32_t run = sat_add(ucum, excl), before = run, ev = kNoEvent;
-                int evq = 0;
+                    for (int q = 1; q < 8; q++) cs[q] = __fadd_rn(cs[q - 1], pv[q]);
+                    uint32_t m = 0;
 #pragma unroll
-                for (int q = 0; q < kPerThread; q++) {
-                    const int i = start + lane * kPerThread + q;
-                    if (i >= t0end || ev != kNoEvent) continue;
-                    if (ser[q]) { ev = (uint32_t)i << 1; before = run; evq = q; continue; }
-                    const uint32_t nr = sat_add(run, k[q]);
-                    if (nr >= kBinadeUnits) { ev = (uint32_t)i << 1; before = run; evq = q; continue; }
-                    if (nr >= tr) { ev = ((uint32_t)i << 1) | 1u; evq = q; continue; }
-                    run = nr;
-                }
-                const uint32_t gev = __reduce_min_sync(0xffffffffu, ev);
-                if (gev == kNoEvent) {
-                    if (lane == 0) {
-                        S.ucum = ucum + all;  // no crossing: exact and < 2^24
-                        S.start = min(start + kWarp * kPerThread, t0end);
+                    for (int q = 0; q < 8; q++) m |= (cs[q] >= r ? 1u : 0u) << q;
+                    if (m) {
+                        hit = j + __ffs(m) - 1;
+                        break;
                     }
-                    break;
+                    cum = cs[7];
                 }
-                if (ev == gev) {  // owner of the first event
-                    const int i = (int)(gev >> 1);
-                    if (gev & 1u) {
-                        S.result = i;
-                    } else {
-                        float pe = pt[start + lane * kPerThread];
-#pragma unroll
-                        for (int q = 1; q < kPerThread; q++)
-                            if (q == evq) pe = pt[start + lane * kPerThread + q];
-                        const float cum_prev =
-                            __fmul_rn(__fmul_rn((float)before, pow2i(E - 23 + 64)), pow2i(-64));
-                        const float cum = __fadd_rn(cum_prev, pe);
-                        if (cum >= r) S.result = i;
-                        else { set_binade(S, cum, r, ln_2inv); S.start = i + 1; }
-                    }
+                for (; hit < 0 && j < jend; j++) {
+                    cum = __fadd_rn(cum, pt[j]);
+                    if (cum >= r) hit = j;
                 }
-                __syncwarp();
+                if (hit >= 0) break;
+                if ((__float_as_uint(cum) >> 23) == e0 && cum > 0.0f) break;  // a quiet stretch
             }
+            if (hit >= 0) S.result = hit;
+            else set_binade(S, cum, r, ln_2inv);  // exact: the unit arithmetic resumes from cum
+            S.start = j;
         }
         __syncthreads();
     }
