@@ -978,8 +978,13 @@ def run_ncu_case(cases, rows=16384):
             assert L.ane_cuda_sample_rows(P(logits), r, v, v, P(hist), P(hlen), 1024, P(u), 0.6,
                                           1.2, 256, 0.1, P(tok), sp) == 0
         torch.cuda.synchronize()
-    if "attention" in cases:
-        for B, H, hk, ln, dt in ((16, 32, 8, 4096, torch.float16), (1, 16, 8, 4096, torch.float32)):
+    attn = []
+    if "attention" in cases or "attn_f16" in cases:
+        attn.append((16, 32, 8, 4096, torch.float16))
+    if "attention" in cases or "attn_f32" in cases:
+        attn.append((1, 16, 8, 4096, torch.float32))
+    if attn:
+        for B, H, hk, ln, dt in attn:
             g = torch.Generator(device="cuda").manual_seed(9)
             q = torch.randn(B, H, 128, device="cuda", generator=g).to(dt)
             k = torch.randn(B, ln, hk, 128, device="cuda", generator=g).to(dt)
@@ -990,6 +995,18 @@ def run_ncu_case(cases, rows=16384):
                 ane.decode_attention(q, k, v, st, n, max_len=ln)
             torch.cuda.synchronize()
             del q, k, v
+    if "embed" in cases:
+        # the decode step's first RMSNorm fed by the embedding gather, at prefill rows
+        g = torch.Generator(device="cuda").manual_seed(5)
+        table = (torch.randn(VOCAB, HIDDEN, device="cuda", generator=g) * 0.05).half()
+        ids = torch.randint(0, VOCAB, (rows,), device="cuda", dtype=torch.int32, generator=g)
+        w = torch.rand(HIDDEN, device="cuda", generator=g) + 0.5
+        x = torch.empty(rows, HIDDEN, dtype=torch.float16, device="cuda")
+        out = torch.empty_like(x)
+        for _ in range(2):
+            ane.embedding_rmsnorm(table, ids, w, x=x, out=out)
+        torch.cuda.synchronize()
+        del table, x, out
     if "pack" in cases:
         x = torch.randn(8192, 4096, device="cuda")
         surf = torch.zeros((256, 4096, 32), dtype=torch.int16, device="cuda")
@@ -1011,8 +1028,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--ncu-case", default="",
-                    help="comma list of chain,convert,sampler,attention,pack: run the small profiling "
-                         "case and exit")
+                    help="comma list of chain,convert,sampler,attention (attn_f16, attn_f32),embed,pack: "
+                         "run the small profiling case and exit")
     args = ap.parse_args()
     if args.ncu_case:
         run_ncu_case(set(args.ncu_case.split(",")))
