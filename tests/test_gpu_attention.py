@@ -153,6 +153,40 @@ def test_attention_matches_reference(ane, ref, shape):
     assert np.abs(got[0] - want).max() <= tol
 
 
+# fp32, one sequence alone and the same sequence as row 17 of a batch of
+# 40 with other lengths and starts: both give the oracle's bits (a split's
+# partials and the merge do not depend on the other rows of the batch).
+# Lengths ragged against the 64-key splits, wrapped rings, 8192 keys, 8 q
+# heads per kv head, head_dim 64, max_len below the capacity.
+BATCH_POSITION_CASES = [
+    # H, Hk, hd, cap, start, len, max_len
+    (16, 8, 128, 4096, 0, 4096, None),
+    (16, 8, 128, 4096, 1000, 4000, None),
+    (16, 8, 128, 8192, 77, 8192, None),
+    (16, 8, 128, 1024, 1000, 129, None),
+    (16, 8, 128, 4096, 5, 700, 1000),
+    (64, 8, 128, 2048, 2000, 2047, None),
+    (32, 8, 64, 3000, 2999, 3000, None),
+    (24, 8, 128, 512, 500, 300, None),
+]
+
+
+@pytest.mark.parametrize("case", BATCH_POSITION_CASES, ids=lambda c: f"H{c[0]}k{c[1]}d{c[2]}c{c[3]}l{c[5]}")
+def test_attention_same_bits_alone_and_in_a_batch(ane, oracle, case):
+    H, hk, hd, cap, start, length, max_len = case
+    rng = np.random.default_rng(zlib.crc32(repr(("cl", case)).encode()))
+    q, k, v, st, ln = make_case(rng, 1, H, hk, hd, cap, [start], [length], "f32")
+    want = oracle.decode_attention(q, k, v, st, ln)
+    one = run_gpu(ane, q, k, v, st, ln, "f32", max_len=max_len)
+    assert np.array_equal(bits(one), bits(want)), int((bits(one) != bits(want)).sum())
+    B = 40  # the sequence as row 17 of a batch
+    qb, kb_, vb, stb, lnb = make_case(rng, B, H, hk, hd, cap, list(rng.integers(0, cap, B)),
+                                      list(rng.integers(1, length + 1, B)), "f32")
+    qb[17], kb_[17], vb[17], stb[17], lnb[17] = q[0], k[0], v[0], st[0], ln[0]
+    many = run_gpu(ane, qb, kb_, vb, stb, lnb, "f32", max_len=max_len)
+    assert np.array_equal(bits(many[17]), bits(one[0]))
+
+
 def test_attention_caller_workspace_two_calls(ane, oracle):
     """A caller workspace full of garbage (it needs no clearing: only the
     call in flight keeps its split partials there) gives the same bits as
