@@ -5,8 +5,11 @@
 // Pass 0  the row's repetition window goes into a shared-memory hash
 //         (id -> count) and a vocabulary bitmap; each distinct id's logit is
 //         penalised once (rep, then freq), as sampling.cpp:17-42 does.
-// Pass 1  max of the penalised logits (argmax for temperature <= 0).
-//         max(fl(a * inv_t)) = fl(max(a) * inv_t) since rounding is monotone.
+// Pass 1  max of the penalised logits (argmax for temperature <= 0), back
+//         to front, eight 16-byte groups in flight per thread; max.NaN
+//         propagates a NaN logit into the result, which is all the NaN rule
+//         needs.  max(fl(a * inv_t)) = fl(max(a) * inv_t) since rounding is
+//         monotone.
 // Pass 2  e = exp(d), d = fl(fl(a * inv_t) - max), summed in the pinned order
 //         of 1024 "virtual threads": group g of 4 consecutive elements belongs
 //         to virtual thread g % 1024, which adds its elements in increasing
@@ -25,11 +28,14 @@
 //         after it.  The first element whose running sum reaches r (in
 //         units: ceil(r / U)) is the token.
 //         Elements with d < T(E) = ln(U / (2 inv)) - 1e-4 have p < U / 2:
-//         they add 0 units, are no tie and cannot leave the binade, so their
-//         exp is never evaluated.  U only grows along the row, so an element
-//         found insignificant stays so.  The exps that are needed are
-//         compacted per warp through shared memory, so a warp evaluates
-//         ceil(significant / 32) exps per slot instead of one per element.
+//         they add 0 units, are no tie and cannot leave the binade.  U only
+//         grows along the row, so an element found insignificant stays so.
+//         A tile's elements are tested against a logit floor xl with
+//         d(xl) < T(E) (a superset of the significant ones, one compare per
+//         element); each warp compacts its candidates in element order into
+//         shared memory and evaluates their p once.  The first tile, where
+//         cum leaves its binade every few elements, is summed serially in
+//         fp32 by one thread until the binade holds for 256 elements.
 #include <atomic>
 
 #include "ane_common.cuh"
@@ -42,6 +48,7 @@ constexpr int kSampWarps = kSampThreads / kWarp;   // 16
 constexpr int kVirtThreads = 1024;                 // pinned softmax-sum order
 constexpr int kPerThread = 8;                      // CDF elements per thread per tile
 constexpr int kTile = kSampThreads * kPerThread;   // 4096
+constexpr int kMaxSweep = 8;                       // groups of 4 in flight per thread, max pass
 constexpr int kMaxWindow = 4096;
 constexpr uint32_t kSat = 1u << 30;                // saturation of unit counts
 constexpr uint32_t kBinadeUnits = 1u << 24;
@@ -63,6 +70,12 @@ struct SampArgs {
     bool vec;  // rows 16-byte aligned and vocab % 4 == 0
 };
 
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) {
     const uint32_t s = a + b;  // a, b <= kSat, no wrap
     return s < kSat ? s : kSat;
@@ -78,10 +91,11 @@ struct RowSmem {
     uint32_t ucum;   // running sum in units of U
     int E;           // binade exponent; U = 2^(E-23)
     uint32_t tr;     // ceil(r / U), saturated
-    float td;        // significance threshold on d for this binade
     int start;       // first element still to scan
-    uint32_t ev;     // event code of this round
+    float xl;        // CDF candidates: logits above xl (a superset of the significant ones)
     int result;
+    uint32_t ev_before[kSampWarps];  // per warp: units before its first event
+    float ev_p[kSampWarps];          //           and that element's p
 };
 
 // --- penalties -------------------------------------------------------------
@@ -221,17 +235,43 @@ __device__ __forceinline__ void classify(float p, int E, uint32_t& k, bool& tie,
     k = q + (rem > half ? 1u : 0u);
 }
 
-// Sets the binade state of S from an exact fp32 running sum `cum`.
-__device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, double ln_2inv) {
+// The CDF scan's candidate floor for a binade: a logit xl with d(xl) < td,
+// d(v) = fl(fl(v * inv_t) - max).  d does not decrease with v, so every
+// logit v <= xl has d(v) < td: it is insignificant.  xl comes from td with a
+// margin that covers the two roundings of d, and is checked; -inf (every
+// element a candidate) if the check fails.  t_inv = 1 / inv_t in double.
+__device__ __forceinline__ float candidate_floor(float td, float inv_t, float neg_m, double t_inv) {
+    if (!(td > -INFINITY)) return -INFINITY;
+    const double t = (double)td, n = (double)neg_m;
+    const double delta = 0x1p-21 * (fabs(t - n) + fabs(n) + fabs(t)) + 0x1p-140;
+    const double y = (t - n - delta) * t_inv;
+    const float x = __double2float_rd(y - fabs(y) * 0x1p-40);
+    if (!(x == x)) return -INFINITY;
+    return __fadd_rn(__fmul_rn(x, inv_t), neg_m) < td ? x : -INFINITY;
+}
+
+// The scan state in one binade [2^E, 2^(E+1)) of the running sum.
+struct Binade {
+    uint32_t ucum;  // running sum in units of U = 2^(E-23)
+    int E;
+    uint32_t tr;    // ceil(r / U), saturated
+    float td;       // significance threshold on d
+    float xl;       // candidate floor on the logits
+};
+
+// The binade state of an exact fp32 running sum `cum`.
+__device__ __forceinline__ Binade binade_of(float cum, float r, double ln_2inv, float inv_t, float neg_m,
+                                            double t_inv) {
+    Binade B;
     const uint32_t b = __float_as_uint(cum);
     int e = (int)((b >> 23) & 0xFFu) - 127;
     if (e < -126) e = -126;
-    S.E = e;
+    B.E = e;
     // cum / U: exact integer below 2^24
     const int pe = (int)((b >> 23) & 0xFFu);
     const uint32_t m = pe ? ((b & 0x7FFFFFu) | 0x800000u) : (b & 0x7FFFFFu);
     const int s = (pe ? pe : 1) - 127 - e;  // 0 for normals and for e = -126 subnormals
-    S.ucum = m << s;
+    B.ucum = m << s;
     // ceil(r / U)
     const uint32_t rb = __float_as_uint(r);
     const int re = (int)((rb >> 23) & 0xFFu);
@@ -243,14 +283,25 @@ __device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, doubl
     else if (rs >= 0) tr = rm << rs;
     else if (-rs >= 25) tr = 1;
     else tr = (rm + (1u << -rs) - 1u) >> -rs;
-    S.tr = tr < kSat ? tr : kSat;
+    B.tr = tr < kSat ? tr : kSat;
     // d < td  =>  exp(d) * inv < U / 2 with room for the exp's and the
     // product's rounding (relative 2^-21) and for rounding td itself.  Below
     // U / 2 = 2^-126 a product near U / 2 would be subnormal and its rounding
     // no longer relative: no element is skipped there.
     // ln(U / (2 inv)) = (E - 23) ln 2 - ln(2 inv), ln(2 inv) computed once per row
-    S.td = e - 24 >= -126 ? (float)((double)(e - 23) * 0.69314718055994530942 - ln_2inv - 1e-4)
+    B.td = e - 24 >= -126 ? (float)((double)(e - 23) * 0.69314718055994530942 - ln_2inv - 1e-4)
                           : -INFINITY;
+    B.xl = candidate_floor(B.td, inv_t, neg_m, t_inv);
+    return B;
+}
+
+__device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, double ln_2inv, float inv_t,
+                                           float neg_m, double t_inv) {
+    const Binade B = binade_of(cum, r, ln_2inv, inv_t, neg_m, t_inv);
+    S.E = B.E;
+    S.ucum = B.ucum;
+    S.tr = B.tr;
+    S.xl = B.xl;
 }
 
 __global__ void __launch_bounds__(kSampThreads, 2)
@@ -258,7 +309,7 @@ sample_rows_kernel(const SampArgs a) {
     pdl_begin();
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ RowSmem S;
-    __shared__ float cbuf[kSampWarps][kWarp * kPerThread];       // compacted d, then p
+    __shared__ __align__(16) float cbuf[kSampWarps][kWarp * kPerThread];  // candidates: logit, then p
     __shared__ uint16_t cidx[kSampWarps][kWarp * kPerThread];    // their tile-local indices
     const int64_t row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -323,26 +374,25 @@ sample_rows_kernel(const SampArgs a) {
     // counted on the side.
     // (back to front: the exp-sum pass then starts on the lines read last,
     // which are still in L2)
+    // max.NaN: a NaN logit makes mx NaN (the NaN rule below); otherwise mx
+    // is the largest penalised logit.  kMaxSweep groups in flight per thread.
     float mx = -INFINITY;
-    bool nan_seen = false;
-    const int nsweep = (ngroups + 4 * kSampThreads - 1) / (4 * kSampThreads);
+    const int nsweep = (ngroups + kMaxSweep * kSampThreads - 1) / (kMaxSweep * kSampThreads);
     for (int sw = nsweep - 1; sw >= 0; sw--) {
-        const int g0 = sw * 4 * kSampThreads;
-        float v[4][4];
+        const int g0 = sw * kMaxSweep * kSampThreads;
+        float v[kMaxSweep][4];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
+        for (int u = 0; u < kMaxSweep; u++) {
             const int g = g0 + u * kSampThreads + tid;
             if (g < ngroups) load4(a, lrow, P, g * 4, v[u]);
             else v[u][0] = v[u][1] = v[u][2] = v[u][3] = -INFINITY;
         }
 #pragma unroll
-        for (int u = 0; u < 4; u++)
+        for (int u = 0; u < kMaxSweep; u++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                mx = fmaxf(mx, v[u][e]);
-                nan_seen |= v[u][e] != v[u][e];
-            }
+            for (int e = 0; e < 4; e++) mx = max_nan(mx, v[u][e]);
     }
+    bool nan_seen = mx != mx;
     nan_seen = __syncthreads_or(nan_seen);
     mx = block_max(mx, S);
     const float inv_t = __fdiv_rn(1.0f, a.temperature);
@@ -369,9 +419,14 @@ sample_rows_kernel(const SampArgs a) {
         const float2 e01 = pinned_expf_nonpos2(make_float2(d[0], d[1]));
         const float2 e23 = pinned_expf_nonpos2(make_float2(d[2], d[3]));
         const float e[4] = {e01.x, e01.y, e23.x, e23.y};
+        if (g * 4 + 3 < a.vocab) {
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-            if (g * 4 + j < a.vocab) acc = __fadd_rn(acc, e[j]);
+            for (int j = 0; j < 4; j++) acc = __fadd_rn(acc, e[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (g * 4 + j < a.vocab) acc = __fadd_rn(acc, e[j]);
+        }
     };
     for (int g0 = 0; g0 < ngroups; g0 += 2 * kVirtThreads) {
         const int ga = g0 + tid, gb = ga + kSampThreads;
@@ -395,8 +450,9 @@ sample_rows_kernel(const SampArgs a) {
         return;
     }
     const double ln_2inv = log(2.0 * (double)inv);
+    const double t_inv = 1.0 / (double)inv_t;
     if (tid == 0) {
-        set_binade(S, 0.0f, r, ln_2inv);
+        set_binade(S, 0.0f, r, ln_2inv, inv_t, neg_m, t_inv);
         S.start = 0;
         S.result = -1;
     }
@@ -429,17 +485,23 @@ sample_rows_kernel(const SampArgs a) {
             while (j < t0end) {
                 const int jend = min(t0end, j + kWarp * kPerThread);
                 const uint32_t e0 = __float_as_uint(cum) >> 23;
+                // j is a multiple of 8 here; the next chunk's loads are
+                // issued before this chunk's adds
+                float4 n0 = *reinterpret_cast<const float4*>(pt + j);
+                float4 n1 = *reinterpret_cast<const float4*>(pt + j + 4);
                 for (; j + 8 <= jend; j += 8) {
-                    float pv[8], cs[8];
-#pragma unroll
-                    for (int q = 0; q < 8; q++) pv[q] = pt[j + q];
+                    const float pv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+                    const int jn = min(j + 8, kTile - 8);
+                    n0 = *reinterpret_cast<const float4*>(pt + jn);
+                    n1 = *reinterpret_cast<const float4*>(pt + jn + 4);
+                    float cs[8];
                     cs[0] = __fadd_rn(cum, pv[0]);
 #pragma unroll
                     for (int q = 1; q < 8; q++) cs[q] = __fadd_rn(cs[q - 1], pv[q]);
-                    uint32_t m = 0;
+                    if (cs[7] >= r) {  // p >= 0: the running sums do not decrease
+                        uint32_t m = 0;
 #pragma unroll
-                    for (int q = 0; q < 8; q++) m |= (cs[q] >= r ? 1u : 0u) << q;
-                    if (m) {
+                        for (int q = 0; q < 8; q++) m |= (cs[q] >= r ? 1u : 0u) << q;
                         hit = j + __ffs(m) - 1;
                         break;
                     }
@@ -453,181 +515,216 @@ sample_rows_kernel(const SampArgs a) {
                 if ((__float_as_uint(cum) >> 23) == e0 && cum > 0.0f) break;  // a quiet stretch
             }
             if (hit >= 0) S.result = hit;
-            else set_binade(S, cum, r, ln_2inv);  // exact: the unit arithmetic resumes from cum
+            else set_binade(S, cum, r, ln_2inv, inv_t, neg_m, t_inv);  // exact: the unit arithmetic resumes from cum
             S.start = j;
         }
         __syncthreads();
     }
-    float* cb = cbuf[w];
-    uint16_t* ci = cidx[w];
+    // ---- pass 3b: the other tiles, over candidate lists ------------------------
+    // Per tile: each thread tests its 8 logits against the binade's floor
+    // xl (every significant element is a candidate; most elements are not),
+    // each warp compacts its candidates in element order into shared
+    // memory, computes their p once and adds their units for the current
+    // binade (a serial element -- tie or big -- saturates the sum).  One
+    // block prefix of the 16 warp totals gives the tile's total: below tr
+    // and inside the binade, nothing happens in the tile and the state
+    // advances in every thread alike.  Otherwise the first event (serial
+    // element, binade crossing or hit) lies in the first warp whose units
+    // reach the limit; that warp walks its candidates in order to find it,
+    // every thread applies it to its own copy of the state (the real fp32
+    // add, as in the first tile), the warps from the event's on recount
+    // their remaining candidates from the stored p in the new binade, and
+    // so on until the tile is done.
+    float* const cv = cbuf[w];
+    uint16_t* const ci = cidx[w];
     const int ntiles = (a.vocab + kTile - 1) / kTile;
-    // The scan state, held identically by every thread: a tile without an
-    // event (no serial element, no crossing, no hit -- read off the block
-    // total alone) advances it locally with no further barrier; after an
-    // event the owner updates S and every thread reloads it.
     uint32_t st_ucum = S.ucum, st_tr = S.tr;
     int st_E = S.E, st_start = S.start;
-    float st_td = S.td;
+    float st_xl = S.xl;
+    int res = S.result;
     int rp = 0;  // round parity: which wscan buffer
-    for (int tile = S.start / kTile; tile < ntiles && S.result < 0; tile++) {
+    auto units = [](float p, int E) {
+        uint32_t k;
+        bool tie, big;
+        classify(p, E, k, tie, big);
+        return (tie || big) ? kSat : k;
+    };
+    // sum of the warp's units (every lane gets it, in `mine`), then the block
+    // prefix: wpre = units of the warps before this one; returns all 16
+    // warps' total
+    auto block_units = [&](uint32_t& mine, uint32_t& wpre) {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mine = sat_add(mine, __shfl_xor_sync(0xffffffffu, mine, off));
+        if (lane == 0) S.wscan[rp][w] = mine;
+        __syncthreads();
+        uint32_t t = lane < kSampWarps ? S.wscan[rp][lane] : 0u;
+        rp ^= 1;
+#pragma unroll
+        for (int off = 1; off < kSampWarps; off <<= 1) {
+            const uint32_t o = __shfl_up_sync(0xffffffffu, t, off);
+            if (lane >= off) t = sat_add(t, o);
+        }
+        wpre = __shfl_sync(0xffffffffu, t, (w + 31) & 31);
+        if (w == 0) wpre = 0;
+        return __shfl_sync(0xffffffffu, t, kSampWarps - 1);
+    };
+    for (int tile = st_start / kTile; tile < ntiles && res < 0; tile++) {
         const int tbase = tile * kTile;
         const int base = tbase + tid * kPerThread;
-        float d[kPerThread];
-#pragma unroll
-        for (int h = 0; h < kPerThread / 4; h++) {
-            float v[4];
-            load4(a, lrow, P, base + 4 * h, v);
-#pragma unroll
-            for (int e = 0; e < 4; e++) d[4 * h + e] = __fadd_rn(__fmul_rn(v[e], inv_t), neg_m);
-        }
-        // compact the significant elements of the warp, in element order
-        const float td0 = st_td;
-        uint32_t sig = 0;
-#pragma unroll
-        for (int e = 0; e < kPerThread; e++)
-            if (base + e < a.vocab && d[e] >= td0) sig |= 1u << e;
-        const int cnt = __popc(sig);
-        int incl = cnt;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int o = __shfl_up_sync(0xffffffffu, incl, off);
-            if (lane >= off) incl += o;
-        }
-        const int nw = __shfl_sync(0xffffffffu, incl, 31);
-        int pos = incl - cnt;
-#pragma unroll
-        for (int e = 0; e < kPerThread; e++)
-            if ((sig >> e) & 1u) {
-                cb[pos] = d[e];
-                ci[pos] = (uint16_t)(tid * kPerThread + e);
-                pos++;
-            }
-        __syncwarp();
-        // exps of the compacted items, two per lane at a time (packed)
-        for (int j = lane; j < nw; j += 2 * kWarp) {
-            const int j2 = j + kWarp < nw ? j + kWarp : j;
-            const float2 ex = pinned_expf_nonpos2(make_float2(cb[j], cb[j2]));
-            const float p0 = __fmul_rn(ex.x, inv), p1 = __fmul_rn(ex.y, inv);
-            cb[j] = p0;  // lane l owns items l + 64m and l + 32 + 64m
-            if (j2 != j) cb[j2] = p1;
-        }
-        __syncwarp();
-        // lane l takes the contiguous items [l*c, l*c + c)
-        const int c = (nw + kWarp - 1) / kWarp;
-        const int first = lane * c;
-        const int mine = max(0, min(c, nw - first));
-        float pv[kPerThread];
-        int li[kPerThread];
-#pragma unroll
-        for (int q = 0; q < kPerThread; q++) {
-            pv[q] = q < mine ? cb[first + q] : 0.0f;
-            li[q] = q < mine ? (int)ci[first + q] : 0x7FFF;
-        }
-
         const int tile_end = min(tbase + kTile, a.vocab);
-        while (true) {
-            const uint32_t ucum = st_ucum;
-            const int E = st_E, start = st_start;
-            const uint32_t tr = st_tr;
-            uint32_t k[kPerThread];
-            bool ser[kPerThread], valid[kPerThread];
-            uint32_t kt = 0;
+        uint32_t msk = 0;
+        {
+            float v[kPerThread];
 #pragma unroll
-            for (int q = 0; q < kPerThread; q++) {
-                k[q] = 0;
-                ser[q] = false;
-                valid[q] = q < c && q < mine && tbase + li[q] >= start;
-                // warp-uniform skip of slots that no lane holds any more
-                if (__any_sync(0xffffffffu, valid[q])) {
-                    bool tie, big;
-                    classify(pv[q], E, k[q], tie, big);
-                    ser[q] = valid[q] && (tie || big);
-                    if (!valid[q]) k[q] = 0;
-                    kt = sat_add(kt, ser[q] ? kSat : k[q]);
-                }
-            }
-            uint32_t inc = kt;
+            for (int h = 0; h < kPerThread / 4; h++) load4(a, lrow, P, base + 4 * h, &v[4 * h]);
+#pragma unroll
+            for (int e = 0; e < kPerThread; e++) msk |= (v[e] > st_xl ? 1u : 0u) << e;
+            const int lo = min(max(st_start - base, 0), kPerThread);
+            const int hi = min(max(a.vocab - base, 0), kPerThread);
+            msk &= ((1u << hi) - 1u) & ~((1u << lo) - 1u);
+            const int cnt = __popc(msk);
+            int incl = cnt;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
-                const uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
-                if (lane >= off) inc = sat_add(inc, o);
+                const int o = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += o;
             }
-            if (lane == 31) S.wscan[rp][w] = inc;  // warp total
-            __syncthreads();
-            // prefix over the warp totals: lane j holds warp j's total
-            uint32_t wt = lane < kSampWarps ? S.wscan[rp][lane] : 0u;
-            rp ^= 1;
+            int pos = incl - cnt;
 #pragma unroll
-            for (int off = 1; off < kSampWarps; off <<= 1) {
-                const uint32_t o = __shfl_up_sync(0xffffffffu, wt, off);
-                if (lane >= off) wt = sat_add(wt, o);
+            for (int e = 0; e < kPerThread; e++)
+                if ((msk >> e) & 1u) {
+                    cv[pos] = v[e];
+                    ci[pos] = (uint16_t)(tid * kPerThread + e);
+                    pos++;
+                }
+            msk = (uint32_t)__shfl_sync(0xffffffffu, incl, 31);  // the warp's candidate count
+        }
+        const int nw = (int)msk;
+        __syncwarp();
+        // p of each candidate (kept in cv), this lane's units: items lane, lane + 32, ...
+        uint32_t mine = 0;
+        for (int j0 = 0; j0 < nw; j0 += 2 * kWarp) {
+            const int ja = j0 + lane, jb = ja + kWarp;
+            const float da = ja < nw ? __fadd_rn(__fmul_rn(cv[ja], inv_t), neg_m) : -INFINITY;
+            const float db = jb < nw ? __fadd_rn(__fmul_rn(cv[jb], inv_t), neg_m) : -INFINITY;
+            const float2 ex = pinned_expf_nonpos2(make_float2(da, db));
+            if (ja < nw) {
+                const float p = __fmul_rn(ex.x, inv);
+                cv[ja] = p;
+                mine = sat_add(mine, units(p, st_E));
             }
-            const uint32_t all = __shfl_sync(0xffffffffu, wt, kSampWarps - 1);
-            const uint32_t tot = sat_add(ucum, all);
-            if (tot < tr && tot < kBinadeUnits) {
-                // no event in the tile (a serial element saturates `all`):
-                // the same update in every thread, no barrier
+            if (jb < nw) {
+                const float p = __fmul_rn(ex.y, inv);
+                cv[jb] = p;
+                mine = sat_add(mine, units(p, st_E));
+            }
+        }
+        __syncwarp();
+        uint32_t wpre;
+        uint32_t all = block_units(mine, wpre);
+        while (true) {
+            const uint32_t tot = sat_add(st_ucum, all);
+            if (tot < st_tr && tot < kBinadeUnits) {  // no event in the rest of the tile
                 st_ucum = tot;  // exact and < 2^24
                 st_start = tile_end;
                 break;
             }
-            uint32_t wpre = __shfl_sync(0xffffffffu, wt, (w + 31) & 31);
-            if (w == 0) wpre = 0;
-            uint32_t excl = __shfl_up_sync(0xffffffffu, inc, 1);
-            if (lane == 0) excl = 0;
-            uint32_t run = sat_add(ucum, sat_add(wpre, excl));
-            // first event of this lane: serial (tie / big / binade crossing) or hit
-            uint32_t ev = kNoEvent, before = run;
-            int evq = 0;
+            // The first event lies in the first warp whose units reach tr or
+            // leave the binade (a serial element saturates them): only that
+            // warp walks its candidates in order to find it.
+            uint32_t run = sat_add(st_ucum, wpre);
+            const uint32_t lim = st_tr < kBinadeUnits ? st_tr : kBinadeUnits;
+            const bool ev_warp = run < lim && sat_add(run, mine) >= lim;
+            uint32_t ev = kNoEvent, before = 0;
+            float pe = 0.0f;
+            for (int j0 = 0; ev_warp && j0 < nw; j0 += kWarp) {
+                const int j = j0 + lane;
+                const bool valid = j < nw && tbase + (int)ci[j] >= st_start;
+                const float p = valid ? cv[j] : 0.0f;
+                uint32_t k;
+                bool tie, big;
+                classify(p, st_E, k, tie, big);
+                const bool ser = valid && (tie || big);
+                const uint32_t kk = valid ? (ser ? kSat : k) : 0u;
+                uint32_t inc = kk;
 #pragma unroll
-            for (int q = 0; q < kPerThread; q++) {
-                if (q >= c) break;  // warp-uniform
-                if (!valid[q] || ev != kNoEvent) continue;
-                const uint32_t local = (uint32_t)li[q];
-                if (ser[q]) { ev = local << 1; before = run; evq = q; continue; }
-                const uint32_t nr = sat_add(run, k[q]);
-                if (nr >= kBinadeUnits) { ev = local << 1; before = run; evq = q; continue; }
-                if (nr >= tr) { ev = (local << 1) | 1u; evq = q; continue; }
-                run = nr;
+                for (int off = 1; off < 32; off <<= 1) {
+                    const uint32_t o = __shfl_up_sync(0xffffffffu, inc, off);
+                    if (lane >= off) inc = sat_add(inc, o);
+                }
+                uint32_t ex = __shfl_up_sync(0xffffffffu, inc, 1);
+                if (lane == 0) ex = 0;
+                const uint32_t r0 = sat_add(run, ex);  // units before this candidate
+                uint32_t e = kNoEvent;
+                if (valid) {
+                    const uint32_t local = (uint32_t)ci[j] << 1;
+                    if (ser) {
+                        e = local;
+                    } else {
+                        const uint32_t nr = sat_add(r0, k);
+                        if (nr >= kBinadeUnits) e = local;
+                        else if (nr >= st_tr) e = local | 1u;
+                    }
+                }
+                const uint32_t bal = __ballot_sync(0xffffffffu, e != kNoEvent);
+                if (bal) {  // candidates ascend with the lanes: the lowest lane is first
+                    const int src = __ffs(bal) - 1;
+                    ev = __shfl_sync(0xffffffffu, e, src);
+                    before = __shfl_sync(0xffffffffu, r0, src);
+                    pe = __shfl_sync(0xffffffffu, p, src);
+                    break;
+                }
+                run = sat_add(run, __shfl_sync(0xffffffffu, inc, 31));
             }
-            const uint32_t wmin = __reduce_min_sync(0xffffffffu, ev);
-            if (lane == 0) S.red_u[w] = wmin;
+            if (lane == 0) {
+                S.red_u[w] = ev;
+                S.ev_before[w] = before;
+                S.ev_p[w] = pe;
+            }
             __syncthreads();
-            const uint32_t gev =
-                __reduce_min_sync(0xffffffffu, lane < kSampWarps ? S.red_u[lane] : kNoEvent);
-            if (gev == kNoEvent) {  // cannot happen (the test above took those tiles); kept safe
-                st_ucum = ucum + all;
+            // the first event over the warps, applied by every thread to its
+            // own copy of the state (the next writes of these slots come
+            // after the barrier of the recount below)
+            const uint32_t wev = lane < kSampWarps ? S.red_u[lane] : kNoEvent;
+            const uint32_t gev = __reduce_min_sync(0xffffffffu, wev);
+            if (gev == kNoEvent) {  // cannot happen (the total above had one); kept safe
+                st_ucum = tot < kBinadeUnits ? tot : st_ucum;
                 st_start = tile_end;
                 break;
             }
-            if (ev == gev) {  // owner of the first event
-                const int i = tbase + (int)(gev >> 1);
-                if (gev & 1u) {
-                    S.result = i;
-                } else {
-                    float pe = pv[0];
-#pragma unroll
-                    for (int q = 1; q < kPerThread; q++)
-                        if (q == evq) pe = pv[q];
-                    // before * 2^(E-23), exact: two power-of-two scalings; then a real fp32 add
-                    const float cum_prev =
-                        __fmul_rn(__fmul_rn((float)before, pow2i(E - 23 + 64)), pow2i(-64));
-                    const float cum = __fadd_rn(cum_prev, pe);
-                    if (cum >= r) S.result = i;
-                    else { set_binade(S, cum, r, ln_2inv); S.start = i + 1; }
-                }
+            const int i = tbase + (int)(gev >> 1);
+            if (gev & 1u) {
+                res = i;
+                break;
             }
-            __syncthreads();
-            if (S.result >= 0) break;
-            st_ucum = S.ucum;
-            st_tr = S.tr;
-            st_E = S.E;
-            st_start = S.start;
-            st_td = S.td;
+            const int ow = __ffs(__ballot_sync(0xffffffffu, wev == gev)) - 1;
+            // before * 2^(E-23), exact: two power-of-two scalings; then a real fp32 add
+            const float cum_prev =
+                __fmul_rn(__fmul_rn((float)S.ev_before[ow], pow2i(st_E - 23 + 64)), pow2i(-64));
+            const float cum = __fadd_rn(cum_prev, S.ev_p[ow]);
+            if (cum >= r) {
+                res = i;
+                break;
+            }
+            {
+                const Binade B = binade_of(cum, r, ln_2inv, inv_t, neg_m, t_inv);
+                st_ucum = B.ucum;
+                st_tr = B.tr;
+                st_E = B.E;
+                st_xl = B.xl;
+                st_start = i + 1;
+            }
+            // the tile's remaining candidates recounted in the new binade
+            // (the warps before the event's have none left)
+            mine = 0;
+            if (w >= ow)
+                for (int j = lane; j < nw; j += kWarp)
+                    if (tbase + (int)ci[j] >= st_start) mine = sat_add(mine, units(cv[j], st_E));
+            all = block_units(mine, wpre);
         }
-        if (S.result >= 0) break;
+        if (res >= 0) break;
     }
-    if (tid == 0) a.out[row] = S.result >= 0 ? S.result : a.vocab - 1;
+    if (tid == 0) a.out[row] = res >= 0 ? res : a.vocab - 1;
 }
 
 // softmax over rows in place (core/cpu_ops.cpp:83-99) with the pinned sum.

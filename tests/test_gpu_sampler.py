@@ -63,6 +63,23 @@ def test_sampler_vocab_sizes(ane, oracle, vocab):
         assert np.array_equal(got, want), (temp, np.nonzero(got != want)[0][:10])
 
 
+@pytest.mark.parametrize("base", [-1000.0, -20.0, 0.0, 25.0, 1000.0])
+def test_sampler_offsets_scales_temperatures(ane, oracle, base):
+    """The CDF scan tests logits against a floor derived from the binade's
+    significance threshold (d = fl(fl(v / T) - max)): offsets that make the
+    max large, near zero or negative, spreads from flat to peaked, and
+    temperatures from cold to hot, with every u from 0 to just below 1."""
+    rng = np.random.default_rng(int(base) + 5000)
+    vocab, rows = 20000, 12
+    for sigma in (0.05, 3.0, 80.0):
+        logits = (base + rng.standard_normal((rows, vocab)) * sigma).astype(np.float32)
+        u = np.linspace(0, 0.99999994, rows).astype(np.float32)
+        for temp in (0.05, 0.6, 3.0):
+            got = run(ane, logits, u, temperature=temp, repetition_penalty=1.0)
+            want = oracle.sample_rows(logits, u, temperature=temp, rep=1.0)
+            assert np.array_equal(got, want), (sigma, temp, np.nonzero(got != want)[0][:10])
+
+
 def test_sampler_edge_distributions(ane, oracle):
     vocab = 50000
     rows = []
