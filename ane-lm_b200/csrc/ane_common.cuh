@@ -158,30 +158,18 @@ __device__ __forceinline__ float rcp_approx(float x) {
 
 // Packed fp32 pairs (sm_100 f32x2): two independent IEEE operations per
 // instruction, each rounded to nearest even with subnormals kept -- the same
-// bits as __fmul_rn / __fadd_rn / __fsub_rn / __fmaf_rn element by element
-// (checked on the B200 over 2^20 random pairs, specials included).
+// bits as __fmul_rn / __fmaf_rn element by element (checked on the B200 over
+// 2^20 random pairs, specials included).
 // The pairs are built and split inside the asm (mov.b64 {lo, hi}), so no
-// value is reinterpreted through a pointer.
+// value is reinterpreted through a pointer.  There is no packed add here on
+// purpose: the compiler contracts a packed multiply feeding a packed add or
+// subtract into a packed fma despite the .rn modifiers (seen as 1-ulp and
+// cancellation differences against the reference), so sums after a packed
+// multiply are taken with scalar __fadd_rn / __fsub_rn.
 __device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
     float2 d;
     asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
         " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
-    float2 d;
-    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
-        " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 sub2_rn(float2 a, float2 b) {
-    float2 d;
-    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
-        " sub.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
         : "=f"(d.x), "=f"(d.y)
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
