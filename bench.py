@@ -313,7 +313,7 @@ def max_over_ranks(torch, dist, world, v):
     return out if isinstance(v, (list, tuple)) else out[0]
 
 
-def time_e2e_chain(torch, ane, rows, steps, chunks=8):
+def time_e2e_chain(torch, ane, rows, steps, chunks=16):
     """The same chain through the public C ABI with HOST buffers: every step
     copies its inputs (x, d, qkv, gate, up) from pinned memory to the device,
     runs the three kernels and copies the outputs (x, y, qkv, h) back, in
@@ -931,7 +931,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e_ms, 3),
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-                    "note": "pinned host buffers, each rank its own rows in 8 blocks over 2 streams"},
+                    "note": "pinned host buffers, each rank its own rows in 16 blocks over 2 streams"},
             "gpu_launches": 3 * args.steps,
             "clocks": clocks,
             "extra": extras,
