@@ -88,6 +88,19 @@ __device__ __forceinline__ void pdl_begin() {
     asm volatile("griddepcontrol.launch_dependents;" :::);
 }
 
+// Bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
+// multiple of 16).  A kernel issues it for its first inputs BEFORE
+// pdl_begin(), so those bytes start to come from DRAM while the previous
+// grid on the stream drains.  This is safe whatever that grid writes: a
+// prefetch only fills L2, the point of coherence of the GPU's global memory,
+// so a line fetched before the previous grid wrote it is updated there by
+// that write, and the kernel's own loads, all issued after
+// griddepcontrol.wait, see the written value.  Nothing is loaded into the
+// SM (no L1 fill, no register), and no value a thread reads changes.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t s, Args... args) {

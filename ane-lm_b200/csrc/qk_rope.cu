@@ -75,12 +75,24 @@ constexpr int kRowWarps = 4;
 template <typename T, int GL, int D, bool KV>
 __global__ void __launch_bounds__(kRowWarps * kWarp, KV ? 4 : 8)
 qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim) {
-    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     constexpr int HPW = kWarp / GL;                  // heads per iteration
     constexpr int HALF = GL * V;                     // rot_dim / 2 = head_dim / 2
     constexpr int CPL = HALF >= 32 ? HALF / 32 : V;  // cos/sin computed per lane
+    {
+        // the row's q and k heads toward L2 while the previous grid drains,
+        // when they are contiguous (16-byte aligned, sizes multiples of 16
+        // bytes on this path)
+        const int64_t r = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+        if ((threadIdx.x & 31) == 0 && r < a.rows) {
+            if (a.n_q > 0 && a.q_head_stride == 2 * HALF)
+                prefetch_l2((const S*)a.q + r * a.q_row_stride, (uint32_t)(a.n_q * 2 * HALF * sizeof(S)));
+            if (a.n_kv > 0 && a.k_head_stride == 2 * HALF)
+                prefetch_l2((const S*)a.k + r * a.k_row_stride, (uint32_t)(a.n_kv * 2 * HALF * sizeof(S)));
+        }
+    }
+    pdl_begin();
     __shared__ __align__(16) float s_freq[HALF];
     __shared__ __align__(16) float s_w[2][2 * HALF];
     for (int i = threadIdx.x; i < HALF; i += blockDim.x) s_freq[i] = fr.f[i];

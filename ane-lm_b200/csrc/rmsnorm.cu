@@ -23,10 +23,17 @@ rmsnorm_reg_kernel(typename T::storage* x, int64_t xs,
                    const typename T::storage* __restrict__ d, int64_t ds,
                    typename T::storage* out, int64_t os, const float* __restrict__ w,
                    int64_t rows, int dim, float eps) {
-    pdl_begin();
     constexpr int V = T::kVec;
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+    // the row's x and d toward L2 while the previous grid drains (16-byte
+    // aligned rows, dim * size a multiple of 16 on this path)
+    if (lane == 0 && row < rows) {
+        const uint32_t bytes = (uint32_t)dim * sizeof(typename T::storage);
+        prefetch_l2(x + row * xs, bytes);
+        if constexpr (HAS_D) prefetch_l2(d + row * ds, bytes);
+    }
+    pdl_begin();
     if (row >= rows) return;
     const int nvec = dim / V;
     typename T::storage* xr = x + row * xs;

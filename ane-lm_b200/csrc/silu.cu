@@ -137,10 +137,18 @@ constexpr size_t act_bulk_smem() { return (size_t)kBulkStages * NIN * kBulkTile;
 template <typename T, int MODE>
 __global__ void __launch_bounds__(kActThreads)
 act_bulk_kernel(const ActArgs p, int64_t ntiles, unsigned int* flags) {
-    pdl_begin();
     using S = typename T::storage;
     constexpr int V = T::kVec;
     constexpr int NIN = MODE == SILU ? 1 : 2;
+    // the CTA's first tiles toward L2 while the previous grid drains
+    if (threadIdx.x == 0)
+        for (int k = 0; k < kBulkStages; k++)
+            if (blockIdx.x + (int64_t)k * gridDim.x < ntiles) {
+                const int64_t off = (blockIdx.x + (int64_t)k * gridDim.x) * kBulkTile;
+                prefetch_l2(static_cast<const char*>(p.a) + off, kBulkTile);
+                if constexpr (NIN == 2) prefetch_l2(static_cast<const char*>(p.b) + off, kBulkTile);
+            }
+    pdl_begin();
     constexpr int STEPS = kBulkTile / (kActThreads * 16);  // 16-byte vectors per thread and tile
     extern __shared__ __align__(128) unsigned char smem[];  // [stage][input][kBulkTile]
     __shared__ __align__(8) uint64_t full[kBulkStages];
