@@ -206,12 +206,17 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
                     const float w0[4] = {t0.x, t0.y, t0.z, t0.w};
                     const float w1[4] = {t1.x, t1.y, t1.z, t1.w};
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {  // (x * inv) * w, two elements per multiply
-                        const float2 t = mul2_rn(mul2_rn(make_float2(x0[4 * q4 + e], x1[4 * q4 + e]),
-                                                         make_float2(inv, inv)),
-                                                 make_float2(w0[e], w1[e]));
-                        x0[4 * q4 + e] = t.x;
-                        x1[4 * q4 + e] = t.y;
+                    for (int e = 0; e < 4; e += 2) {  // (x * inv) * w, neighbouring elements paired
+                        const float2 t0 = mul2_rn(mul2_rn(make_float2(x0[4 * q4 + e], x0[4 * q4 + e + 1]),
+                                                          make_float2(inv, inv)),
+                                                  make_float2(w0[e], w0[e + 1]));
+                        const float2 t1 = mul2_rn(mul2_rn(make_float2(x1[4 * q4 + e], x1[4 * q4 + e + 1]),
+                                                          make_float2(inv, inv)),
+                                                  make_float2(w1[e], w1[e + 1]));
+                        x0[4 * q4 + e] = t0.x;
+                        x0[4 * q4 + e + 1] = t0.y;
+                        x1[4 * q4 + e] = t1.x;
+                        x1[4 * q4 + e + 1] = t1.y;
                     }
                 }
             }
@@ -224,14 +229,20 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
             } else if (live) {
                 float y0[V], y1[V];
 #pragma unroll
-                for (int e = 0; e < V; e++) {
-                    // v0 c - v1 s and v1 c + v0 s: the four products two per
-                    // multiply, the sum and difference by scalar operations (a
-                    // packed multiply feeding a packed add may be contracted)
-                    const float2 pc = mul2_rn(make_float2(x0[e], x1[e]), make_float2(cs[e], cs[e]));
-                    const float2 ps = mul2_rn(make_float2(x1[e], x0[e]), make_float2(sn[e], sn[e]));
-                    y0[e] = __fsub_rn(pc.x, ps.x);
-                    y1[e] = __fadd_rn(pc.y, ps.y);
+                for (int e = 0; e < V; e += 2) {
+                    // v0 c - v1 s and v1 c + v0 s for elements e and e + 1:
+                    // each product pairs neighbouring elements (operands that
+                    // already sit in neighbouring registers), the sums and
+                    // differences are scalar (a packed multiply feeding a
+                    // packed add may be contracted)
+                    const float2 c2 = make_float2(cs[e], cs[e + 1]), s2 = make_float2(sn[e], sn[e + 1]);
+                    const float2 a0 = make_float2(x0[e], x0[e + 1]), a1 = make_float2(x1[e], x1[e + 1]);
+                    const float2 p0c = mul2_rn(a0, c2), p1s = mul2_rn(a1, s2);
+                    const float2 p1c = mul2_rn(a1, c2), p0s = mul2_rn(a0, s2);
+                    y0[e] = __fsub_rn(p0c.x, p1s.x);
+                    y0[e + 1] = __fsub_rn(p0c.y, p1s.y);
+                    y1[e] = __fadd_rn(p1c.x, p0s.x);
+                    y1[e + 1] = __fadd_rn(p1c.y, p0s.y);
                 }
                 const uint4 p0 = pack<T>(y0), p1 = pack<T>(y1);
                 S* q = head_ptr(h);
