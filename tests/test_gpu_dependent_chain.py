@@ -165,3 +165,69 @@ def test_decode_step_kv_write_then_attention(ane):
     torch.cuda.synchronize()
     assert torch.equal(out.view(torch.int16), want.view(torch.int16))
     del g
+
+
+def test_prefill_chain_dependent_fp16_bulk_sizes(ane):
+    """The prefill chain at sizes that take the register RMSNorm, the
+    row-per-warp QK-norm + RoPE and the bulk-copy SiLU-gate -- the three
+    kernels that prefetch their first inputs into L2 before waiting for the
+    previous kernel -- with each kernel reading what the one before it is
+    still writing: x += d and y = rmsnorm(x); QK-norm + RoPE in place on y;
+    h = silu(y) * x over the whole rows (contiguous, so SiLU takes the bulk
+    path).  Three chains back to back with no synchronisation, and the chain
+    replayed from a captured graph, give the same bits as the same calls
+    with a device synchronisation after each."""
+    import torch
+    R, H, nq, nkv, hd = 2048, 4096, 24, 8, 128  # (24 + 8) x 128 = H: q and k heads over y
+    g = torch.Generator(device="cpu").manual_seed(44)
+    x0 = torch.randn(R, H, generator=g).half().cuda()
+    d = torch.randn(R, H, generator=g).half().cuda()
+    w = (1 + 0.1 * torch.randn(H, generator=g)).float().cuda()
+    qw = (1 + 0.1 * torch.randn(hd, generator=g)).float().cuda()
+    kw = (1 + 0.1 * torch.randn(hd, generator=g)).float().cuda()
+    pos = (torch.arange(R, dtype=torch.int32) % 512).cuda()
+
+    def chain(x, y, h, sync):
+        ane.residual_rmsnorm(x, d, w, out=y)
+        if sync:
+            torch.cuda.synchronize()
+        ane.qk_norm_rope(y, qw, kw, pos, nq, nkv, hd)
+        if sync:
+            torch.cuda.synchronize()
+        ane.silu_mul(y, x, out=h)
+        if sync:
+            torch.cuda.synchronize()
+
+    xs, ys, hs = x0.clone(), torch.empty_like(x0), torch.empty_like(x0)
+    want = []
+    for _ in range(3):
+        chain(xs, ys, hs, sync=True)
+        want.append((xs.clone(), ys.clone(), hs.clone()))
+    x, y, h = x0.clone(), torch.empty_like(x0), torch.empty_like(x0)
+    got = []
+    for _ in range(3):  # the next chain's RMSNorm reads the x this one wrote
+        chain(x, y, h, sync=False)
+        got.append((x.clone(), y.clone(), h.clone()))  # torch copies, launched without the attribute
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(zip(got, want)):
+        for name, t, e in zip(("x", "y", "h"), a, b):
+            assert torch.equal(t.view(torch.int16), e.view(torch.int16)), (i, name)
+
+    # replayed from a graph, the inputs restored inside it
+    s = torch.cuda.Stream()
+    x, y, h = x0.clone(), torch.empty_like(x0), torch.empty_like(x0)
+    with torch.cuda.stream(s):
+        chain(x, y, h, sync=False)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=s):
+        x.copy_(x0)
+        chain(x, y, h, sync=False)
+    for _ in range(3):
+        y.zero_()
+        h.zero_()
+        gr.replay()
+    torch.cuda.synchronize()
+    for name, t, e in zip(("x", "y", "h"), (x, y, h), want[0]):
+        assert torch.equal(t.view(torch.int16), e.view(torch.int16)), ("graph", name)
+    del gr
