@@ -119,57 +119,122 @@ def cpu_model():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and throttle reasons sampled DURING the timed region.
 
+    A thread reads NVML (the library nvidia-smi reports from) every ~2 ms
+    from the moment the region starts until it ends, so that a region of a
+    few milliseconds -- the multi-GPU steps -- still gets samples; without
+    NVML bindings an `nvidia-smi -lms 100` process is the fallback, waited
+    for until it prints before the region starts."""
+
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_s: float = 0.002):
         self.gpu = gpu_index
+        self.period = period_s
+        self.samples = []  # (sm MHz, reason bits)
+        self.max_mhz = None
+        self.source = None
+        self._nvml = None
+        self._thread = None
+        self._stop = None
         self.proc = None
+        self.out = ""
+
+    def _start_nvml(self):
+        try:
+            import threading
+
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            sample = lambda: (float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)),  # noqa: E731
+                              int(reasons(h)))
+            sample()
+        except Exception:
+            return False
+        self._nvml = pynvml
+        self._stop = threading.Event()
+
+        def run():
+            while True:
+                try:
+                    self.samples.append(sample())
+                except Exception:
+                    pass
+                if self._stop.wait(self.period):
+                    break
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        self.source = "nvml, every 2 ms"
+        return True
 
     def __enter__(self):
+        if self._start_nvml():
+            return self
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline()  # sampling has begun
+            self.out = first
+            self.source = "nvidia-smi, every 100 ms"
         except Exception:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.out = ""
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
-            time.sleep(0.25)
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                rest, _ = self.proc.communicate(timeout=5)
+                self.out += rest
             except Exception:
                 self.proc.kill()
         return False
 
     def summary(self):
-        sms, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in (self.out or "").splitlines():
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sms.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() in ("active", "1"):
-                    reasons.add(nm)
+        sms, reasons = [], set()
+        if self.source and self.source.startswith("nvml"):
+            for mhz, bits in self.samples:
+                sms.append(mhz)
+                reasons.update(nm for nm, b in self.REASONS if bits & b)
+        else:
+            names = [nm for nm, _ in self.REASONS]
+            for ln in (self.out or "").splitlines():
+                parts = [p.strip() for p in ln.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sms.append(float(parts[1]))
+                    self.max_mhz = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, v in zip(names, parts[5:9]):
+                    if v.lower() in ("active", "1"):
+                        reasons.add(nm)
         if not sms:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0,
+                    "source": self.source}
         sms.sort()
-        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sms)}
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(sms), "source": self.source}
 
 
 # ---------------------------------------------------------------------------
@@ -188,6 +253,38 @@ def _setup_gpu(world):
     import ane_lm_cuda
     ane_lm_cuda.lib()  # fails loudly when the library is missing
     return torch, ane_lm_cuda, rank, local
+
+
+def parse_cpulist(text):
+    """The CPU set of a Linux cpulist string ("0-3,8,10-11")."""
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.update(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def bind_near_gpu(torch, dev, sysfs="/sys/bus/pci/devices"):
+    """Keep this process on the host CPUs next to GPU `dev` (its PCI
+    device's local_cpulist), so that the pinned host buffers it allocates
+    afterwards are placed on that NUMA node by first touch and the
+    host<->device copies of one rank do not cross the socket interconnect.
+    Returns the cpulist applied, or None when there is nothing to narrow
+    (one NUMA node, or the topology is not visible)."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        pid = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+        with open(os.path.join(sysfs, pid, "local_cpulist")) as f:
+            text = f.read().strip()
+        want = parse_cpulist(text) & os.sched_getaffinity(0)
+    except (OSError, AttributeError, ValueError):
+        return None
+    if not want or want == os.sched_getaffinity(0):
+        return None
+    os.sched_setaffinity(0, want)
+    return text
 
 
 def make_chain_inputs(torch, row0, rows, hidden, nq, nkv, hd, inter, seq, device="cuda"):
@@ -903,6 +1000,10 @@ def run_ours(args):
     torch.cuda.empty_cache()
 
     e2e_steps = max(2, min(5, args.steps))
+    # with several ranks on a multi-socket host, each rank's pinned buffers
+    # and copies stay on its GPU's socket (the CPU baseline, rank 0 at N = 1,
+    # keeps every host thread)
+    bound = bind_near_gpu(torch, local) if world > 1 else None
     _barrier(dist, world)
     e_ms, h2d, d2h, e_launches = time_e2e_chain(torch, ane, nrows, e2e_steps)
     e_ms = max_over_ranks(torch, dist, world, e_ms)
@@ -931,7 +1032,8 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 3), "unit": "GB/s", "ms_per_step": round(e_ms, 3),
                     "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
-                    "note": "pinned host buffers, each rank its own rows in 16 blocks over 2 streams"},
+                    "note": "pinned host buffers, each rank its own rows in 16 blocks over 2 streams"
+                            + (f"; rank 0 bound to CPUs {bound} (its GPU's NUMA node)" if bound else "")},
             "gpu_launches": 3 * args.steps,
             "clocks": clocks,
             "extra": extras,
