@@ -1,6 +1,9 @@
 // sampler.cu -- batched sample_token (core/sampling.cpp:10-66) and softmax
-// (core/cpu_ops.cpp:83-99), one 512-thread CTA per row, two CTAs per SM so
-// that a batch of up to 2 x SMs rows runs in a single wave.
+// (core/cpu_ops.cpp:83-99), one CTA per row: 512 threads, two CTAs per SM,
+// so that a batch of up to 2 x SMs rows runs in a single wave; a batch of
+// at most one row per SM (a row-sharded batch on several GPUs) takes one
+// 1024-thread CTA per row instead.  The summation orders below are those of
+// 1024 virtual threads whatever the CTA size, so both give the same bits.
 //
 // Pass 0  the row's repetition window goes into a shared-memory hash
 //         (id -> count) and a vocabulary bitmap; each distinct id's logit is
@@ -43,11 +46,11 @@
 
 namespace ane {
 
-constexpr int kSampThreads = 512;
-constexpr int kSampWarps = kSampThreads / kWarp;   // 16
+constexpr int kSampThreads = 512;                 // softmax, and sampling with more rows than SMs
+constexpr int kSampThreadsWide = 1024;            // sampling with at most one row per SM
+constexpr int kMaxSampWarps = kSampThreadsWide / kWarp;
 constexpr int kVirtThreads = 1024;                 // pinned softmax-sum order
 constexpr int kPerThread = 8;                      // CDF elements per thread per tile
-constexpr int kTile = kSampThreads * kPerThread;   // 4096
 constexpr int kMaxSweep = 8;                       // groups of 4 in flight per thread, max pass
 constexpr int kMaxWindow = 4096;
 constexpr uint32_t kSat = 1u << 30;                // saturation of unit counts
@@ -84,8 +87,8 @@ __device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) {
 // Shared state of one row.
 struct RowSmem {
     float red_f[kVirtThreads / kWarp];
-    uint32_t red_u[kSampWarps];
-    uint32_t wscan[2][kSampWarps];  // warp totals, alternating by round
+    uint32_t red_u[kMaxSampWarps];
+    uint32_t wscan[2][kMaxSampWarps];  // warp totals, alternating by round
     float bcast_f;
     // CDF state
     uint32_t ucum;   // running sum in units of U
@@ -94,8 +97,8 @@ struct RowSmem {
     int start;       // first element still to scan
     float xl;        // CDF candidates: logits above xl (a superset of the significant ones)
     int result;
-    uint32_t ev_before[kSampWarps];  // per warp: units before its first event
-    float ev_p[kSampWarps];          //           and that element's p
+    uint32_t ev_before[kMaxSampWarps];  // per warp: units before its first event
+    float ev_p[kMaxSampWarps];          //           and that element's p
 };
 
 // --- penalties -------------------------------------------------------------
@@ -139,7 +142,9 @@ __device__ __forceinline__ void load4(const SampArgs& a, const float* row, const
 }
 
 // --- block reductions --------------------------------------------------------
+template <int NT>
 __device__ __forceinline__ float block_max(float v, RowSmem& S) {
+    constexpr int kSampWarps = NT / kWarp;
     for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) S.red_f[w] = v;
@@ -153,17 +158,19 @@ __device__ __forceinline__ float block_max(float v, RowSmem& S) {
     return S.bcast_f;
 }
 
-// The pinned order over 1024 virtual threads: acc_lo belongs to virtual
-// thread t, acc_hi to t + 512.  Butterfly inside each virtual warp, then over
-// the 32 virtual-warp sums (virtual warp w is real warp w for acc_lo and real
-// warp w - 16 for acc_hi).
-__device__ __forceinline__ float block_sum_pinned(float acc_lo, float acc_hi, RowSmem& S) {
-    const float lo = butterfly_sum(acc_lo, kWarp);
-    const float hi = butterfly_sum(acc_hi, kWarp);
+// The pinned order over 1024 virtual threads: thread t of an NT-thread CTA
+// plays virtual threads t, t + NT, ... (acc[v] is virtual thread t + v NT).
+// Butterfly inside each virtual warp (virtual warp w + v NT / 32 is real
+// warp w's acc[v]), then over the 32 virtual-warp sums -- the same order for
+// every NT.
+template <int NT>
+__device__ __forceinline__ float block_sum_pinned(const float (&acc)[kVirtThreads / NT], RowSmem& S) {
+    constexpr int VPT = kVirtThreads / NT, NW = NT / kWarp;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        S.red_f[w] = lo;
-        S.red_f[w + kSampWarps] = hi;
+#pragma unroll
+    for (int v = 0; v < VPT; v++) {
+        const float s = butterfly_sum(acc[v], kWarp);
+        if (lane == 0) S.red_f[w + v * NW] = s;
     }
     __syncthreads();
     if (w == 0) {
@@ -175,12 +182,13 @@ __device__ __forceinline__ float block_sum_pinned(float acc_lo, float acc_hi, Ro
 }
 
 // --- pass 0: window -> hash + bitmap ------------------------------------------
+template <int NT>
 __device__ Penalty build_penalties(const SampArgs& a, int64_t row, const float* lrow,
                                    uint32_t* bitmap, int32_t* keys, int32_t* counts, float* vals) {
     const int nwords = (a.vocab + 31) >> 5;
     const int slots = 1 << a.slots_log2;
-    for (int i = threadIdx.x; i < nwords; i += kSampThreads) bitmap[i] = 0u;
-    for (int i = threadIdx.x; i < slots; i += kSampThreads) { keys[i] = -1; counts[i] = 0; }
+    for (int i = threadIdx.x; i < nwords; i += NT) bitmap[i] = 0u;
+    for (int i = threadIdx.x; i < slots; i += NT) { keys[i] = -1; counts[i] = 0; }
     __syncthreads();
     Penalty P{bitmap, keys, vals, (uint32_t)(slots - 1), 32 - a.slots_log2};
     if (a.hist && a.hist_len) {
@@ -189,7 +197,7 @@ __device__ Penalty build_penalties(const SampArgs& a, int64_t row, const float* 
         int start = hl - a.ctx;
         if (start < 0) start = 0;
         const int32_t* h = a.hist + row * a.hs;
-        for (int j = start + threadIdx.x; j < hl; j += kSampThreads) {
+        for (int j = start + threadIdx.x; j < hl; j += NT) {
             const int32_t tok = __ldg(h + j);
             if (tok < 0 || tok >= a.vocab) continue;
             uint32_t s = slot_of(tok, P.shift);
@@ -203,7 +211,7 @@ __device__ Penalty build_penalties(const SampArgs& a, int64_t row, const float* 
         }
     }
     __syncthreads();
-    for (int s = threadIdx.x; s < slots; s += kSampThreads) {
+    for (int s = threadIdx.x; s < slots; s += NT) {
         const int32_t tok = keys[s];
         if (tok < 0) continue;
         float x = lrow[tok];
@@ -304,13 +312,30 @@ __device__ __forceinline__ void set_binade(RowSmem& S, float cum, float r, doubl
     S.xl = B.xl;
 }
 
-__global__ void __launch_bounds__(kSampThreads, 2)
+// Dynamic shared memory of sample_rows_kernel: the window hash (keys,
+// counts, values: 12 B per slot), the vocabulary bitmap, then (16-byte
+// aligned) the per-warp candidate lists: NT / 32 x 256 logits-then-p (4 B)
+// and tile-local indices (2 B).
+__host__ __device__ constexpr size_t cand_offset(int slots, int vocab) {
+    return (((size_t)slots * 12 + (size_t)((vocab + 31) / 32) * 4) + 15) & ~(size_t)15;
+}
+__host__ __device__ constexpr size_t samp_smem(int nt, int slots, int vocab) {
+    return cand_offset(slots, vocab) + (size_t)(nt / kWarp) * kWarp * kPerThread * 6;
+}
+
+// NT = 512: two CTAs per SM (a batch of up to 2 x SMs rows in one wave);
+// NT = 1024: one CTA per SM, for batches of at most one row per SM.  Every
+// order the result depends on is the same for both.
+template <int NT>
+__global__ void __launch_bounds__(NT, NT == kSampThreads ? 2 : 1)
 sample_rows_kernel(const SampArgs a) {
+    constexpr int kSampThreads = NT;
+    constexpr int kSampWarps = NT / kWarp;
+    constexpr int kTile = NT * kPerThread;
+    constexpr int VPT = kVirtThreads / NT;  // virtual threads of the pinned sum per thread
     pdl_begin();
     extern __shared__ __align__(16) unsigned char dyn[];
     __shared__ RowSmem S;
-    __shared__ __align__(16) float cbuf[kSampWarps][kWarp * kPerThread];  // candidates: logit, then p
-    __shared__ uint16_t cidx[kSampWarps][kWarp * kPerThread];    // their tile-local indices
     const int64_t row = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int slots = 1 << a.slots_log2;
@@ -318,8 +343,13 @@ sample_rows_kernel(const SampArgs a) {
     int32_t* counts = keys + slots;
     float* vals = reinterpret_cast<float*>(counts + slots);
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(vals + slots);
+    // candidates (logit, then p) and their tile-local indices, after the bitmap
+    const size_t cand_off = cand_offset(slots, a.vocab);
+    float (*const cbuf)[kWarp * kPerThread] = reinterpret_cast<float (*)[kWarp * kPerThread]>(dyn + cand_off);
+    uint16_t (*const cidx)[kWarp * kPerThread] = reinterpret_cast<uint16_t (*)[kWarp * kPerThread]>(
+        dyn + cand_off + sizeof(float) * kSampWarps * kWarp * kPerThread);
     const float* lrow = a.logits + row * a.ls;
-    const Penalty P = build_penalties(a, row, lrow, bitmap, keys, counts, vals);
+    const Penalty P = build_penalties<NT>(a, row, lrow, bitmap, keys, counts, vals);
     const int ngroups = (a.vocab + 3) >> 2;
 
     // ---- greedy: first maximum (core/sampling.cpp:45-52) ----
@@ -394,7 +424,7 @@ sample_rows_kernel(const SampArgs a) {
     }
     bool nan_seen = mx != mx;
     nan_seen = __syncthreads_or(nan_seen);
-    mx = block_max(mx, S);
+    mx = block_max<NT>(mx, S);
     const float inv_t = __fdiv_rn(1.0f, a.temperature);
     const float neg_m = -__fmul_rn(mx, inv_t);
     const float r = __ldg(a.uniforms + row);
@@ -411,8 +441,10 @@ sample_rows_kernel(const SampArgs a) {
     // ---- pass 2: pinned sum of exp over the 1024 virtual threads ----
     // Two steps of 1024 groups per iteration, all four loads issued first
     // (64 bytes in flight per thread), then the exps and the adds in order.
-    float acc_lo = 0.0f, acc_hi = 0.0f;
-    auto add4 = [&](const float (&v)[4], int g, float& acc) {
+    float acc[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; v++) acc[v] = 0.0f;
+    auto add4 = [&](const float (&v)[4], int g, float& ac) {
         float d[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) d[j] = __fadd_rn(__fmul_rn(v[j], inv_t), neg_m);
@@ -421,28 +453,34 @@ sample_rows_kernel(const SampArgs a) {
         const float e[4] = {e01.x, e01.y, e23.x, e23.y};
         if (g * 4 + 3 < a.vocab) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) acc = __fadd_rn(acc, e[j]);
+            for (int j = 0; j < 4; j++) ac = __fadd_rn(ac, e[j]);
         } else {
 #pragma unroll
             for (int j = 0; j < 4; j++)
-                if (g * 4 + j < a.vocab) acc = __fadd_rn(acc, e[j]);
+                if (g * 4 + j < a.vocab) ac = __fadd_rn(ac, e[j]);
         }
     };
+    // Two steps of 1024 groups per iteration, every load issued first;
+    // virtual thread tid + v NT takes group g0 + tid + v NT, then the same
+    // group of the second step (its groups in increasing order).
     for (int g0 = 0; g0 < ngroups; g0 += 2 * kVirtThreads) {
-        const int ga = g0 + tid, gb = ga + kSampThreads;
-        const int gc = ga + kVirtThreads, gd = gb + kVirtThreads;
-        float va[4], vb[4], vc[4], vd[4];
-        if (ga < ngroups) load4(a, lrow, P, ga * 4, va);
-        if (gb < ngroups) load4(a, lrow, P, gb * 4, vb);
-        if (gc < ngroups) load4(a, lrow, P, gc * 4, vc);
-        if (gd < ngroups) load4(a, lrow, P, gd * 4, vd);
-        // virtual thread t: groups ga then gc; t + 512: gb then gd
-        if (ga < ngroups) add4(va, ga, acc_lo);
-        if (gb < ngroups) add4(vb, gb, acc_hi);
-        if (gc < ngroups) add4(vc, gc, acc_lo);
-        if (gd < ngroups) add4(vd, gd, acc_hi);
+        float vv[2][VPT][4];
+#pragma unroll
+        for (int st = 0; st < 2; st++)
+#pragma unroll
+            for (int v = 0; v < VPT; v++) {
+                const int g = g0 + st * kVirtThreads + v * NT + tid;
+                if (g < ngroups) load4(a, lrow, P, g * 4, vv[st][v]);
+            }
+#pragma unroll
+        for (int st = 0; st < 2; st++)
+#pragma unroll
+            for (int v = 0; v < VPT; v++) {
+                const int g = g0 + st * kVirtThreads + v * NT + tid;
+                if (g < ngroups) add4(vv[st][v], g, acc[v]);
+            }
     }
-    const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
+    const float inv = __fdiv_rn(1.0f, block_sum_pinned<NT>(acc, S));
 
     // ---- pass 3: exact parallel inverse-CDF scan over significant elements ----
     if (!(r > 0.0f)) {  // cum >= r holds after the first element
@@ -738,7 +776,7 @@ softmax_rows_kernel(float* x, int n, int64_t stride) {
     float mx = -INFINITY;
     for (int g = tid; g < ngroups; g += kSampThreads)
         for (int e = 0; e < 4 && g * 4 + e < n; e++) mx = fmaxf(mx, row[g * 4 + e]);
-    const float neg_m = -block_max(mx, S);
+    const float neg_m = -block_max<kSampThreads>(mx, S);
     // x - max is <= 0 or NaN (a NaN element, +inf - inf, or -inf + inf when
     // every element is -inf): NaN stays NaN through the exp, as in the
     // reference's vvexpf, and then makes the sum and every output NaN
@@ -759,7 +797,8 @@ softmax_rows_kernel(float* x, int n, int64_t stride) {
                 acc_hi = __fadd_rn(acc_hi, v);
             }
     }
-    const float inv = __fdiv_rn(1.0f, block_sum_pinned(acc_lo, acc_hi, S));
+    const float accs[2] = {acc_lo, acc_hi};
+    const float inv = __fdiv_rn(1.0f, block_sum_pinned<kSampThreads>(accs, S));
     for (int i = tid; i < n; i += kSampThreads) row[i] = __fmul_rn(row[i], inv);
 }
 
@@ -791,26 +830,33 @@ int ane_cuda_sample_rows(const float* logits, int64_t rows, int vocab, int64_t l
                     (long long)window, kMaxWindow);
     int slots_log2 = 5;
     while ((1 << slots_log2) < 2 * window) slots_log2++;
-    const size_t smem = (size_t)(1 << slots_log2) * 12 + (size_t)((vocab + 31) / 32) * 4;
-    constexpr size_t kMaxDyn = 180 * 1024;  // plus 16 KB of static shared memory
+    // at most one row per SM: one 1024-thread CTA each; else 512-thread CTAs,
+    // two per SM (the results do not depend on the choice)
+    constexpr size_t kMaxDyn = 225 * 1024;  // plus about 1 KB of static shared memory
+    const bool wide = rows <= (int64_t)sm_count() &&
+                      samp_smem(kSampThreadsWide, 1 << slots_log2, vocab) <= kMaxDyn;
+    const size_t smem = samp_smem(wide ? kSampThreadsWide : kSampThreads, 1 << slots_log2, vocab);
     if (smem > kMaxDyn) return fail(ANE_CUDA_ERR_UNSUPPORTED, "sample_rows: vocab %d too large", vocab);
-    // the attribute is set once per device (setting it twice is harmless,
-    // so concurrent first calls need no lock)
-    static std::atomic<int> configured[64];
+    // the attribute is set once per device and kernel (setting it twice is
+    // harmless, so concurrent first calls need no lock)
+    static std::atomic<int> configured[64][2];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
         return fail(ANE_CUDA_ERR_CUDA, "sample_rows: no current device");
-    if (!configured[dev].load(std::memory_order_acquire)) {
-        cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDyn);
+    if (!configured[dev][wide].load(std::memory_order_acquire)) {
+        cudaError_t e = wide ? cudaFuncSetAttribute(sample_rows_kernel<kSampThreadsWide>,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDyn)
+                             : cudaFuncSetAttribute(sample_rows_kernel<kSampThreads>,
+                                                    cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDyn);
         if (e != cudaSuccess)
             return fail(ANE_CUDA_ERR_CUDA, "sample_rows: %s", cudaGetErrorString(e));
-        configured[dev].store(1, std::memory_order_release);
+        configured[dev][wide].store(1, std::memory_order_release);
     }
     SampArgs a{logits, rows, vocab, logits_stride, history, history_len, history_stride, uniforms,
                temperature, repetition_penalty, frequency_penalty, repetition_context, out_tokens,
                slots_log2, vocab % 4 == 0 && logits_stride % 4 == 0 && is_aligned(logits, 16)};
-    launch_pdl(sample_rows_kernel, (unsigned)rows, kSampThreads, smem, as_stream(stream), a);
+    if (wide) launch_pdl(sample_rows_kernel<kSampThreadsWide>, (unsigned)rows, kSampThreadsWide, smem, as_stream(stream), a);
+    else launch_pdl(sample_rows_kernel<kSampThreads>, (unsigned)rows, kSampThreads, smem, as_stream(stream), a);
     return check_launch("sample_rows");
 }
 

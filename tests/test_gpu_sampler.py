@@ -48,6 +48,28 @@ def test_sampler_config4_batch256(ane, oracle):
     assert np.array_equal(got, want), np.nonzero(got != want)[0][:10]
 
 
+def test_sampler_cta_size_does_not_change_tokens(ane, oracle):
+    """A batch of at most one row per SM runs 1024-thread CTAs, a larger one
+    512-thread CTAs; both keep the 1024-virtual-thread orders, so the same
+    rows give the same tokens alone (small batch) and inside a batch of 300
+    (more rows than SMs), all equal to the oracle's.  Greedy rows included."""
+    rng = np.random.default_rng(45)
+    rows, vocab = 300, 151936
+    logits = (rng.standard_normal((rows, vocab)) * 3).astype(np.float32)
+    hist = rng.integers(0, vocab, size=(rows, 1024)).astype(np.int32)
+    hlen = rng.integers(0, 1025, size=rows).astype(np.int32)
+    u = rng.random(rows).astype(np.float32)
+    u[:4] = (0.0, np.float32(0.99999994), 0.5, 0.999)
+    for temp in (0.6, 0.0):
+        big = run(ane, logits, u, hist, hlen, temperature=temp)
+        want = oracle.sample_rows(logits, u, hist, hlen, temperature=temp)
+        assert np.array_equal(big, want), (temp, np.nonzero(big != want)[0][:10])
+        for r0, n in ((0, 1), (5, 32), (40, 100), (150, 148)):
+            small = run(ane, logits[r0:r0 + n], u[r0:r0 + n], hist[r0:r0 + n], hlen[r0:r0 + n],
+                        temperature=temp)
+            assert np.array_equal(small, want[r0:r0 + n]), (temp, r0, n)
+
+
 @pytest.mark.parametrize("vocab", [1, 3, 7, 64, 1001, 4096, 32000, 151936])
 def test_sampler_vocab_sizes(ane, oracle, vocab):
     rng = np.random.default_rng(vocab)
