@@ -133,8 +133,10 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int, period_s: float = 0.002):
+    def __init__(self, gpu_index: int, period_s: float = 0.002, pci_bus_id: str | None = None):
         self.gpu = gpu_index
+        self.pci = pci_bus_id  # NVML is matched by PCI address when given (device
+        #                         numbering may differ from CUDA's)
         self.period = period_s
         self.samples = []  # (sm MHz, reason bits)
         self.max_mhz = None
@@ -151,7 +153,14 @@ class ClockSampler:
 
             import pynvml
             pynvml.nvmlInit()
-            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            h = None
+            if self.pci:
+                try:
+                    h = pynvml.nvmlDeviceGetHandleByPciBusId(self.pci.encode())
+                except Exception:
+                    h = None
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
             self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
             reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
                 pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
@@ -266,6 +275,15 @@ def parse_cpulist(text):
     return cpus
 
 
+def pci_address(torch, dev):
+    """The PCI address ("0000:1b:00.0") of CUDA device `dev`, or None."""
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+    except (AttributeError, RuntimeError, AssertionError, TypeError, ValueError):
+        return None
+
+
 def bind_near_gpu(torch, dev, sysfs="/sys/bus/pci/devices"):
     """Keep this process on the host CPUs next to GPU `dev` (its PCI
     device's local_cpulist), so that the pinned host buffers it allocates
@@ -273,9 +291,10 @@ def bind_near_gpu(torch, dev, sysfs="/sys/bus/pci/devices"):
     host<->device copies of one rank do not cross the socket interconnect.
     Returns the cpulist applied, or None when there is nothing to narrow
     (one NUMA node, or the topology is not visible)."""
+    pid = pci_address(torch, dev)
+    if pid is None:
+        return None
     try:
-        p = torch.cuda.get_device_properties(dev)
-        pid = f"{p.pci_domain_id:04x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
         with open(os.path.join(sysfs, pid, "local_cpulist")) as f:
             text = f.read().strip()
         want = parse_cpulist(text) & os.sched_getaffinity(0)
@@ -382,7 +401,7 @@ def time_device_chain(torch, dist, world, chains, steps, warmup, gpu_index):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(gpu_index) as clk:
+    with ClockSampler(gpu_index, pci_bus_id=pci_address(torch, gpu_index)) as clk:
         start.record()
         for i in range(steps):
             chains[i % n].launch(evs[i])

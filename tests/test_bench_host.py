@@ -74,3 +74,8 @@ def test_clock_summary_from_nvidia_smi_lines():
 def test_clock_summary_without_samples():
     c = bench.ClockSampler(0)
     assert c.summary()["samples"] == 0
+
+
+def test_pci_address():
+    assert bench.pci_address(_fake_torch(dom=0, bus=0x1B, dev=0), 0) == "0000:1b:00.0"
+    assert bench.pci_address(types.SimpleNamespace(cuda=None), 0) is None
