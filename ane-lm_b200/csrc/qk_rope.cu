@@ -63,17 +63,23 @@ struct QkArgs {
 // One warp per row.  The row's heads stream through a ring of D register
 // slots: iteration `it` (HPW heads) is consumed from slot it % D, which is
 // refilled with iteration it + D straight away, so D iterations of loads
-// stay in flight while the warp computes.  D = 1 for the in-place kernel:
-// measured 4% faster than D = 2, whose extra registers cost more than the
-// second iteration of loads in flight bought (the eight resident CTAs per
-// SM already keep enough loads in flight); the KV-writing kernel keeps 2.  Per-row setup (position,
+// stay in flight while the warp computes.  The in-place kernel takes D = 1
+// (eight resident CTAs per SM) when the rows span several waves of CTAs:
+// measured 4-5% faster there than D = 2, whose extra registers cost a
+// resident CTA; when every row's warp is resident at once (one wave of the
+// D = 2 kernel's seven CTAs per SM, 4,096 Qwen3-8B rows on a B200) each warp
+// works through its row alone and D = 2 keeps a second iteration of loads
+// in flight (1.5% faster alone, the chain 1.6%).  A few rows (fewer CTAs
+// than SMs: the batch-1 decode step) take D = 1 again: there the row's own
+// latency decides, and the D = 2 kernel measured 0.6 us slower per token.
+// The KV-writing kernel keeps 2.  Per-row setup (position,
 // cos/sin) is paid once for all heads of the row.  GL (lanes per head) is a
 // template parameter so that every index is a constant; the frequency table
 // and the norm weights are staged once per CTA in shared memory.
 constexpr int kRowWarps = 4;
 
 template <typename T, int GL, int D, bool KV>
-__global__ void __launch_bounds__(kRowWarps * kWarp, KV ? 4 : 8)
+__global__ void __launch_bounds__(kRowWarps * kWarp, KV ? 4 : (D == 2 ? 7 : 8))
 qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim) {
     using S = typename T::storage;
     constexpr int V = T::kVec;
@@ -365,9 +371,13 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s, bool k
     if (fast) {
         const unsigned blocks = (unsigned)((a.rows + kRowWarps - 1) / kRowWarps);
         const bool pow2 = (a.head_dim & (a.head_dim - 1)) == 0;
+        // one full wave: more CTAs than SMs, all resident in the D = 2 kernel
+        const unsigned sms = (unsigned)sm_count();
+        const bool one_wave = blocks > sms && blocks <= 7u * sms;
 #define ANE_QK_ROW(GLV)                                                                          \
     do {                                                                                          \
         if (kv) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, true>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2); \
+        else if (one_wave) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2); \
         else launch_pdl(qk_norm_rope_row_kernel<T, GLV, 1, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2);   \
     } while (0)
         switch (gl_log2) {
