@@ -431,12 +431,15 @@ def max_over_ranks(torch, dist, world, v):
 
 def time_e2e_chain(torch, ane, rows, steps, chunks=16):
     """The same chain through the public C ABI with HOST buffers: every step
-    copies its inputs (x, d, qkv, gate, up) from pinned memory to the device,
-    runs the three kernels and copies the outputs (x, y, qkv, h) back, in
-    `chunks` row blocks over two streams so copies overlap the kernels."""
+    copies its inputs (x, d, the q and k heads, gate, up) from pinned memory
+    to the device, runs the three kernels and copies the outputs (x, y, the
+    q and k heads, h) back, in `chunks` row blocks over two streams so copies
+    overlap the kernels.  The v heads of a qkv row are neither read nor
+    written by the chain, so the host keeps the q and k heads of each row
+    (n_q + n_kv heads) and moves only those."""
     import ctypes as C
     L = ane.lib()
-    width = (NQ + 2 * NKV) * HD
+    width = (NQ + NKV) * HD  # q and k heads
     pin = dict(pin_memory=True)
     g = torch.Generator().manual_seed(7)
     hx = (torch.randn(rows, HIDDEN, generator=g)).half().pin_memory()
