@@ -88,6 +88,80 @@ rmsnorm_reg_kernel(typename T::storage* x, int64_t xs,
     }
 }
 
+// rmsnorm_reg_kernel for rows that fit in a wave or so: d is staged in
+// shared memory by cp.async (each lane its own slots: no barrier), x in
+// registers, so a thread holds 16 chunks instead of 32 and five CTAs fit per
+// SM instead of three.  The same operations in the same order: the same
+// bits.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kNormWarps * kWarp, 5)
+rmsnorm_dsm_kernel(typename T::storage* x, int64_t xs,
+                   const typename T::storage* __restrict__ d, int64_t ds,
+                   typename T::storage* out, int64_t os, const float* __restrict__ w,
+                   int64_t rows, int dim, float eps) {
+    constexpr int V = T::kVec;
+    __shared__ __align__(16) uint4 sd[kNormWarps][VPL][kWarp];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int64_t row = (int64_t)blockIdx.x * kNormWarps + wid;
+    if (lane == 0 && row < rows) {
+        const uint32_t bytes = (uint32_t)dim * sizeof(typename T::storage);
+        prefetch_l2(x + row * xs, bytes);
+        prefetch_l2(d + row * ds, bytes);
+    }
+    pdl_begin();
+    if (row >= rows) return;
+    const int nvec = dim / V;
+    typename T::storage* xr = x + row * xs;
+    typename T::storage* orow = out + row * os;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = lane + i * kWarp;
+        if (c < nvec) cp_async16(&sd[wid][i][lane], d + row * ds + c * V);
+    }
+    cp_async_commit();
+    uint4 xv[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = lane + i * kWarp;
+        if (c < nvec) xv[i] = ld_stream(xr + c * V);
+    }
+    cp_async_wait_pending(0);
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = lane + i * kWarp;
+        if (c < nvec) {
+            float a[V], b[V];
+            unpack<T>(xv[i], a);
+            unpack<T>(sd[wid][i][lane], b);
+#pragma unroll
+            for (int e = 0; e < V; e++) a[e] = __fadd_rn(a[e], b[e]);
+            xv[i] = pack<T>(a);
+            st_stream(xr + c * V, xv[i]);
+            unpack<T>(xv[i], a);  // the norm reads the stored value
+            acc = sumsq_chain<V>(a, acc);
+        }
+    }
+    const float inv = rms_inv(butterfly_sum(acc, kWarp), dim, eps);
+#pragma unroll
+    for (int i = 0; i < VPL; i++) {
+        const int c = lane + i * kWarp;
+        if (c < nvec) {
+            float a[V], wv[V];
+            unpack<T>(xv[i], a);
+            const float4* wp = reinterpret_cast<const float4*>(w + c * V);
+#pragma unroll
+            for (int q = 0; q < V / 4; q++) {
+                const float4 t = __ldg(wp + q);
+                wv[4 * q] = t.x; wv[4 * q + 1] = t.y; wv[4 * q + 2] = t.z; wv[4 * q + 3] = t.w;
+            }
+#pragma unroll
+            for (int e = 0; e < V; e++) a[e] = __fmul_rn(__fmul_rn(a[e], inv), wv[e]);
+            st_stream(orow + c * V, pack<T>(a));
+        }
+    }
+}
+
 // Embedding gather fused with the residual add and RMSNorm after it (the
 // decode step's first op, models/llm/qwen3.cpp:498 then :503 / :516-518):
 // one warp per row, the row in registers.  e = table[id] widened to x's
@@ -287,6 +361,15 @@ static int launch_rmsnorm(void* x, int64_t xs, const void* d, int64_t ds, void* 
     const int per_lane = (dim / V + kWarp - 1) / kWarp;
 #define ANE_NORM_REG(VPL) \
     launch_pdl(rmsnorm_reg_kernel<T, VPL, HAS_D>, blocks, kNormWarps * kWarp, 0, s, xp, xs, dp, ds, op, os, w, rows, dim, eps)
+    // a grid of at most 1.5 waves of the shared-memory form (five CTAs per
+    // SM): there rows in flight and an early start beside the previous
+    // kernel's CTAs count for more than the form's extra shared-memory
+    // accesses (the Qwen3-8B chain at 4,096 rows per GPU +1.2%; 8,192 rows,
+    // 2.8 waves, is faster in registers)
+    if (vec && HAS_D && per_lane == 16 && 2u * blocks <= 3u * 5u * (unsigned)sm_count()) {
+        launch_pdl(rmsnorm_dsm_kernel<T, 16>, blocks, kNormWarps * kWarp, 0, s, xp, xs, dp, ds, op, os, w, rows, dim, eps);
+        return ANE_CUDA_OK;
+    }
     if (vec && per_lane <= 1) ANE_NORM_REG(1);
     else if (vec && per_lane <= 2) ANE_NORM_REG(2);
     else if (vec && per_lane <= 4) ANE_NORM_REG(4);
