@@ -1075,9 +1075,15 @@ def run_ncu_case(cases, rows=16384):
     cur = torch.cuda.current_stream()
     sp = C.c_void_p(cur.cuda_stream)
     P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
-    if "chain" in cases:
-        b = make_chain_inputs(torch, 0, rows, HIDDEN, NQ, NKV, HD, INTER, SEQ)
-        ch = Chain(ane, b, rows, HIDDEN, NQ, NKV, HD, INTER, cur.cuda_stream)
+    # chain: 16,384 rows (several waves of CTAs); chain_small: 4,096 rows,
+    # the rows per GPU at eight GPUs, where the row kernels take their
+    # one-wave forms (RMSNorm with d in shared memory, QK-norm with two
+    # iterations of loads in flight)
+    for case, n in (("chain", rows), ("chain_small", ROWS // 8)):
+        if case not in cases:
+            continue
+        b = make_chain_inputs(torch, 0, n, HIDDEN, NQ, NKV, HD, INTER, SEQ)
+        ch = Chain(ane, b, n, HIDDEN, NQ, NKV, HD, INTER, cur.cuda_stream)
         for _ in range(2):
             ch.launch()
             torch.cuda.synchronize()
@@ -1152,7 +1158,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=6.0)
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--ncu-case", default="",
-                    help="comma list of chain,convert,sampler,attention (attn_f16, attn_f32),embed,pack: "
+                    help="comma list of chain,chain_small,convert,sampler,attention (attn_f16, attn_f32),embed,pack: "
                          "run the small profiling case and exit")
     args = ap.parse_args()
     if args.ncu_case:
