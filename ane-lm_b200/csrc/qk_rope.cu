@@ -2,7 +2,8 @@
 // (models/llm/qwen3.cpp:444-473; core/cpu_ops.cpp:43-80).
 //
 // Fast path (rot_dim == head_dim, head_dim / kVec a power of two in
-// [2, 32], 16-byte aligned rows): one warp per row.  A head is served by
+// [2, 32], 16-byte aligned rows): one warp per row, or, for a few rows (a
+// decode step), one warp per group of HPW heads of a row.  A head is served by
 // GL = chunks/2 lanes; lane l of the group holds chunk l (elements
 // [l*V, l*V+V), first half) and chunk l + GL (the RoPE partners j + half).
 // With that layout
@@ -80,7 +81,8 @@ constexpr int kRowWarps = 4;
 
 template <typename T, int GL, int D, bool KV>
 __global__ void __launch_bounds__(kRowWarps * kWarp, KV ? 4 : (D == 2 ? 7 : 8))
-qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim) {
+qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, const bool pow2_dim,
+                        const int wpr) {
     using S = typename T::storage;
     constexpr int V = T::kVec;
     constexpr int HPW = kWarp / GL;                  // heads per iteration
@@ -90,8 +92,9 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
         // the row's q and k heads toward L2 while the previous grid drains,
         // when they are contiguous (16-byte aligned, sizes multiples of 16
         // bytes on this path)
-        const int64_t r = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
-        if ((threadIdx.x & 31) == 0 && r < a.rows) {
+        const int64_t gw = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+        const int64_t r = gw / wpr;
+        if ((threadIdx.x & 31) == 0 && r < a.rows && gw % wpr == 0) {
             if (a.n_q > 0 && a.q_head_stride == 2 * HALF)
                 prefetch_l2((const S*)a.q + r * a.q_row_stride, (uint32_t)(a.n_q * 2 * HALF * sizeof(S)));
             if (a.n_kv > 0 && a.k_head_stride == 2 * HALF)
@@ -110,13 +113,20 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
     }
     __syncthreads();
     const int lane = threadIdx.x & 31;
-    const int64_t row = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    // a row is wpr warps: warp `part` of them takes the row's iterations
+    // [part * per, part * per + per) (per = the iterations a warp takes)
+    const int64_t gw = (int64_t)blockIdx.x * kRowWarps + (threadIdx.x >> 5);
+    const int64_t row = gw / wpr;
+    const int part = (int)(gw - row * wpr);
     if (row >= a.rows) return;
     const int g = lane / GL;  // head slot of this lane
     const int l = lane % GL;  // lane within the head group
     const int nq = a.n_q, nqk = a.n_q + a.n_kv;
     const int nh = KV ? nqk + a.n_kv : nqk;  // with KV the v heads follow, copy only
-    const int nit = (nh + HPW - 1) / HPW;
+    const int nit_row = (nh + HPW - 1) / HPW;
+    const int per = (nit_row + wpr - 1) / wpr;
+    const int itb = part * per;                         // this warp's first iteration
+    const int nit = min(nit_row, itb + per);            // one past its last
     S* const qrow = (S*)a.q + row * a.q_row_stride;
     S* const krow = (S*)a.k + row * a.k_row_stride;
     const int qhs = a.q_head_stride, khs = a.k_head_stride;
@@ -140,8 +150,8 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
     uint4 lo[D], hi[D];
 #pragma unroll
     for (int d = 0; d < D; d++) {
-        const int h = d * HPW + g;
-        if (h < nh) {
+        const int h = (itb + d) * HPW + g;
+        if (itb + d < nit && h < nh) {
             const S* p = head_ptr(h);
             lo[d] = ld_stream(p + l * V);
             hi[d] = ld_stream(p + HALF + l * V);
@@ -170,7 +180,7 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
 
     const bool norm = a.qw != nullptr;
     const float inv_dim = 1.0f / (float)(2 * HALF);
-    for (int it0 = 0; it0 < nit; it0 += D) {
+    for (int it0 = itb; it0 < nit; it0 += D) {
 #pragma unroll
         for (int d = 0; d < D; d++) {
             if (it0 + d >= nit) break;  // warp-uniform
@@ -191,7 +201,7 @@ qk_norm_rope_row_kernel(const QkArgs a, const __grid_constant__ RopeFreq fr, con
                 for (int e = 0; e < V; e++) { x0[e] = 0.0f; x1[e] = 0.0f; }
             }
             const int hn = h + D * HPW;  // refill the slot D iterations ahead
-            if (hn < nh) {
+            if (it0 + d + D < nit && hn < nh) {
                 const S* q = head_ptr(hn);
                 lo[d] = ld_stream(q + l * V);
                 hi[d] = ld_stream(q + HALF + l * V);
@@ -369,16 +379,24 @@ static int launch_qk(const QkArgs& a, const RopeFreq& fr, cudaStream_t s, bool k
                         "rows, heads and caches", V);
     }
     if (fast) {
-        const unsigned blocks = (unsigned)((a.rows + kRowWarps - 1) / kRowWarps);
         const bool pow2 = (a.head_dim & (a.head_dim - 1)) == 0;
-        // one full wave: more CTAs than SMs, all resident in the D = 2 kernel
         const unsigned sms = (unsigned)sm_count();
-        const bool one_wave = blocks > sms && blocks <= 7u * sms;
+        // Few rows (a decode step): one warp per iteration of HPW heads, so
+        // a row's iterations run side by side instead of one after another,
+        // as long as all those warps fit in one wave of the D = 1 kernel
+        // (eight CTAs of four warps per SM).  The per-row set-up (position,
+        // cos/sin) is then repeated by each of the row's warps.
+        const int hpw = kWarp >> gl_log2;
+        const int nit = (nh + (kv ? a.n_kv : 0) + hpw - 1) / hpw;
+        const int wpr = a.rows * nit <= (int64_t)kRowWarps * 8 * sms ? nit : 1;
+        const unsigned blocks = (unsigned)((a.rows * wpr + kRowWarps - 1) / kRowWarps);
+        // one full wave of whole rows: more CTAs than SMs, all resident in the D = 2 kernel
+        const bool one_wave = wpr == 1 && blocks > sms && blocks <= 7u * sms;
 #define ANE_QK_ROW(GLV)                                                                          \
     do {                                                                                          \
-        if (kv) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, true>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2); \
-        else if (one_wave) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2); \
-        else launch_pdl(qk_norm_rope_row_kernel<T, GLV, 1, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2);   \
+        if (kv) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, true>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2, wpr); \
+        else if (one_wave) launch_pdl(qk_norm_rope_row_kernel<T, GLV, 2, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2, wpr); \
+        else launch_pdl(qk_norm_rope_row_kernel<T, GLV, 1, false>, blocks, kRowWarps * kWarp, 0, s, a, fr, pow2, wpr);   \
     } while (0)
         switch (gl_log2) {
             case 0: ANE_QK_ROW(1); break;
